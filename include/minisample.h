@@ -1,0 +1,165 @@
+/*
+ * libminisample — B200 token sampler behind a plain C ABI.
+ *
+ * This library replaces the token-sampling step of mini.js, `pickToken`
+ * (src/generation.js:71-81), for a [B, V] block of fp32 logits.  Each row gets
+ * exactly what `pickToken` does to one row:
+ *
+ *   1. repetition penalty over the row's id history   (src/generation.js:19-25, :73-75)
+ *   2. greedy argmax when do_sample is false or T<=1e-4 (src/generation.js:51-55, :76)
+ *   3. temperature divide                              (src/generation.js:77-79)
+ *   4. softmax                                         (src/generation.js:9-17)
+ *   5. top-k, top-p and the inverse-CDF draw           (src/generation.js:27-49)
+ *
+ * The reference binds none of this natively: it calls the JS functions above.
+ * The N-API shim (omni.js_b200/csrc/napi_minisample.c) turns
+ * `addon.sample(...)` into `ms_sample` calls; INTEGRATION.md shows the JS side.
+ *
+ * Conventions
+ *   - Every entry point returns 0 on success or a negative MS_ERR_* code and
+ *     leaves a message for ms_last_error().  Nothing traps, nothing falls back
+ *     to a CPU implementation.
+ *   - The caller owns every buffer.  The logits are never modified (the
+ *     reference copies them first, src/generation.js:72).
+ *   - A context is used by one host thread at a time.
+ */
+#ifndef MINISAMPLE_H
+#define MINISAMPLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MS_ABI_VERSION 1
+
+/* Error codes. */
+#define MS_OK            0
+#define MS_ERR_ARG      -1   /* invalid argument (shape, pointer, flag)          */
+#define MS_ERR_CUDA     -2   /* a CUDA runtime call failed                       */
+#define MS_ERR_NCCL     -3   /* an NCCL call failed                              */
+#define MS_ERR_TIMEOUT  -4   /* a bounded wait ran out                           */
+#define MS_ERR_OOM      -5   /* device or pinned allocation failed               */
+#define MS_ERR_STATE    -6   /* context in the wrong state / no device           */
+
+/* ms_sample flags. */
+#define MS_HOST_PTRS      0x1  /* every pointer argument is host memory                */
+#define MS_DEVICE_PTRS    0x2  /* every pointer argument is device memory (ctx device 0) */
+#define MS_ROW_SHARDED    0x4  /* host pointers: split the rows over all ctx devices  */
+#define MS_SYNC           0x8  /* device pointers: synchronize the stream before return */
+#define MS_PROFILE       0x10  /* record CUDA events around each kernel (ms_profile_read) */
+
+/*
+ * Sampling options, one set for the whole batch (the reference applies one
+ * `opts` object to every step, src/generation.js:57-68).  Doubles because the
+ * JS compares doubles: `T <= 0.0001`, `T !== 1.0`, `p !== 1.0`, `acc >= topP`.
+ *   do_sample           0 = greedy                       (src/generation.js:60,76)
+ *   temperature         divide when != 1.0               (src/generation.js:61,77-79)
+ *   top_k               used when 0 < top_k < V          (src/generation.js:62,32)
+ *   top_p               used when top_p != 0 and < 1     (src/generation.js:63,33)
+ *   repetition_penalty  used when != 0, != 1.0 and the row history is non-empty
+ *                       (src/generation.js:64,73).  The caller passes an empty
+ *                       history while `generated.length == 0`.
+ */
+typedef struct ms_params {
+    int32_t do_sample;
+    double  temperature;
+    int32_t top_k;
+    double  top_p;
+    double  repetition_penalty;
+} ms_params;
+
+/*
+ * Optional per-row diagnostics.  Every pointer may be NULL; the non-NULL ones
+ * are host or device memory exactly like the data pointers of the call.
+ *   cand_ids/cand_probs  [B, cand_cap]: the candidates that survive top-k and
+ *                        top-p, in the reference's order (prob desc, id asc),
+ *                        with their fp32 softmax probabilities
+ *   n_cand    [B]  number of surviving candidates (may exceed cand_cap)
+ *   row_max   [B]  max of the tempered logits
+ *   row_sum   [B]  softmax denominator sum(fp32(exp(x - max)))
+ *   total     [B]  fp64 sum of the surviving candidates' probabilities
+ *   row_flags [B]  MS_ROW_* bits below
+ */
+typedef struct ms_diag {
+    int32_t  cand_cap;
+    int32_t* cand_ids;
+    float*   cand_probs;
+    int32_t* n_cand;
+    double*  row_max;
+    double*  row_sum;
+    double*  total;
+    int32_t* row_flags;
+} ms_diag;
+
+#define MS_ROW_GREEDY    0x1   /* greedy argmax row                                  */
+#define MS_ROW_NAN       0x2   /* softmax produced NaN (NaN/+Inf logit, all -Inf row) */
+#define MS_ROW_FULLVOCAB 0x4   /* candidates ranked over the whole vocabulary        */
+#define MS_ROW_SLOWPATH  0x8   /* candidate set resolved by the exact row rescan     */
+
+typedef struct ms_ctx ms_ctx;
+
+/* ABI version of the loaded library (MS_ABI_VERSION). */
+int ms_version(void);
+
+/*
+ * Create a context on `n_devices` CUDA devices (devices == NULL: the current
+ * device only).  Replaces the reference's backend selection,
+ * setBackend('cpu'|'webgl') (src/tensor.js:15-20): the 'cuda' sampler backend
+ * is one context.
+ */
+int ms_create(ms_ctx** out, const int* devices, int n_devices);
+
+/* Free the context, its scratch memory, streams and pinned staging buffers. */
+int ms_destroy(ms_ctx* ctx);
+
+/* Message of the last failed call on this context (never NULL). */
+const char* ms_last_error(ms_ctx* ctx);
+
+/*
+ * Sample one token id per row.  Replaces `pickToken(lastLogits, generated,
+ * inputIds, opts)` (src/generation.js:71-81), applied to each of B rows.
+ *   logits    [B, ld] fp32, ld >= V (row stride in elements)
+ *   hist      concatenated per-row id histories (int32), may be NULL when
+ *             every row is empty; ids outside [0, V) are ignored, repeated ids
+ *             count once (the reference builds a Set, src/generation.js:20)
+ *   hist_off  [B+1] int64 offsets into hist (NULL = no history)
+ *   params    sampling options (host memory always)
+ *   u         [B] fp64 uniforms in [0,1), one per row, standing in for the
+ *             reference's `Math.random()` (src/generation.js:43); read only
+ *             by sampled rows (may be NULL for greedy calls)
+ *   out_ids   [B] int32 sampled ids
+ *   diag      optional diagnostics (NULL = none)
+ *   flags     MS_HOST_PTRS or MS_DEVICE_PTRS, optionally | MS_ROW_SHARDED / MS_SYNC
+ *   stream    cudaStream_t for MS_DEVICE_PTRS calls (NULL = the ctx stream)
+ * With MS_HOST_PTRS the call is synchronous (copies in, sample, copy out),
+ * like the reference's synchronous `generateTokens` (src/generation.js:97-114).
+ */
+int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V, int64_t ld,
+              const int32_t* hist, const int64_t* hist_off, const ms_params* params,
+              const double* u, int32_t* out_ids, ms_diag* diag, int flags,
+              void* stream);
+
+/*
+ * Kernel time of the calls made with MS_PROFILE since the last read, summed
+ * over calls (milliseconds, CUDA events on the launch stream):
+ *   stream_ms    the chunk kernel, which reads every logit once
+ *   finalize_ms  the per-row finalize kernel
+ * Waits for those calls' events.  No reference counterpart: the reference
+ * has no profiling hooks (its demo times with performance.now(),
+ * demo.template.html:230,295).
+ */
+int ms_profile_read(ms_ctx* ctx, double* stream_ms, double* finalize_ms, int64_t* calls);
+
+/*
+ * Bytes of device scratch that ms_sample needs for a [B, V] call with these
+ * params (the context allocates it on first use and keeps it).
+ */
+int ms_scratch_bytes(int64_t B, int64_t V, const ms_params* params, int64_t* out_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MINISAMPLE_H */

@@ -1,0 +1,440 @@
+// libminisample C ABI (include/minisample.h): contexts, scratch, host staging,
+// row sharding over the context's devices, and error reporting.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <array>
+#include <vector>
+
+#include "ms_device.cuh"
+
+namespace ms {
+cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev);
+size_t finalize_smem_bytes();
+}  // namespace ms
+
+namespace {
+
+struct DevState {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  void* scratch = nullptr;  // stats, candidates, penalty bitmap, status word
+  size_t scratch_bytes = 0;
+  void* io = nullptr;       // device copies of host arguments
+  size_t io_bytes = 0;
+  int32_t* status = nullptr;  // status word of the last launch (inside scratch)
+  std::vector<std::array<cudaEvent_t, 3>> prof_pending;  // MS_PROFILE calls not yet read
+  std::vector<std::array<cudaEvent_t, 3>> prof_free;
+};
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct Plan {
+  int mode = ms::kGreedy;
+  int use_pen = 0;
+  int temper = 0;
+  float a = 0.f;
+  int k = 0;
+  int kw = 1;
+  int use_topp = 0;
+  int n_chunks = 1;
+};
+
+Plan make_plan(int64_t V, const ms_params* p, bool have_hist) {
+  Plan P;
+  const double T = p->temperature;
+  const bool greedy = !p->do_sample || T <= 0.0001;
+  const double pen = p->repetition_penalty;
+  P.use_pen = (have_hist && pen != 0.0 && !std::isnan(pen) && pen != 1.0) ? 1 : 0;
+  P.temper = (T != 1.0) ? 1 : 0;
+  P.a = (float)(1.4426950408889634 / T);
+  P.k = p->top_k;
+  P.use_topp = (p->top_p != 0.0 && p->top_p < 1.0) ? 1 : 0;
+  P.n_chunks = (int)((V + ms::kChunk - 1) / ms::kChunk);
+  if (greedy) {
+    P.mode = ms::kGreedy;
+  } else if (P.k > 0 && P.k < V && P.k <= ms::kKmax) {
+    P.mode = ms::kTopK;
+  } else {
+    P.mode = ms::kFull;
+  }
+  const int keff = (P.mode == ms::kTopK) ? P.k : ms::kKSum;
+  P.kw = (keff + 7) / 8;
+  if (P.kw < 1) P.kw = 1;
+  if (P.kw > 32) P.kw = 32;
+  return P;
+}
+
+struct ScratchLayout {
+  size_t stats = 0, cands = 0, penbits = 0, status = 0, total = 0;
+};
+
+ScratchLayout scratch_layout(int64_t B, int64_t V, const Plan& P) {
+  ScratchLayout L;
+  size_t off = 0;
+  L.stats = off;
+  off = align_up(off + (size_t)B * P.n_chunks * sizeof(ms::ChunkStat), 256);
+  L.cands = off;
+  if (P.mode != ms::kGreedy) off = align_up(off + (size_t)B * P.n_chunks * ms::kCap * sizeof(ms::Cand), 256);
+  L.penbits = off;
+  if (P.use_pen && P.mode != ms::kGreedy) off = align_up(off + (size_t)B * ((V + 31) / 32) * 4, 256);
+  L.status = off;
+  off = align_up(off + 256, 256);
+  L.total = off;
+  return L;
+}
+
+}  // namespace
+
+struct ms_ctx {
+  std::vector<DevState> devs;
+  std::string err = "no error";
+};
+
+static int fail(ms_ctx* c, int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  if (c) c->err = buf;
+  return code;
+}
+
+#define MS_CUDA(ctx, call)                                                                      \
+  do {                                                                                          \
+    cudaError_t e_ = (call);                                                                    \
+    if (e_ != cudaSuccess)                                                                      \
+      return fail(ctx, e_ == cudaErrorMemoryAllocation ? MS_ERR_OOM : MS_ERR_CUDA, "%s: %s (%s:%d)", \
+                  #call, cudaGetErrorString(e_), __FILE__, __LINE__);                           \
+  } while (0)
+
+static int ensure(ms_ctx* ctx, void** buf, size_t* have, size_t need) {
+  if (*have >= need) return MS_OK;
+  if (*buf) {
+    cudaFree(*buf);
+    *buf = nullptr;
+    *have = 0;
+  }
+  size_t sz = need + need / 8;
+  MS_CUDA(ctx, cudaMalloc(buf, sz));
+  *have = sz;
+  return MS_OK;
+}
+
+extern "C" {
+
+int ms_version(void) { return MS_ABI_VERSION; }
+
+int ms_create(ms_ctx** out, const int* devices, int n_devices) {
+  if (!out) return MS_ERR_ARG;
+  *out = nullptr;
+  int count = 0;
+  if (cudaGetDeviceCount(&count) != cudaSuccess || count < 1) return MS_ERR_STATE;
+  ms_ctx* c = new ms_ctx();
+  std::vector<int> ids;
+  if (!devices || n_devices <= 0) {
+    int d = 0;
+    cudaGetDevice(&d);
+    ids.push_back(d);
+  } else {
+    for (int i = 0; i < n_devices; i++) {
+      if (devices[i] < 0 || devices[i] >= count) {
+        delete c;
+        return MS_ERR_ARG;
+      }
+      ids.push_back(devices[i]);
+    }
+  }
+  int prev = 0;
+  cudaGetDevice(&prev);
+  for (int d : ids) {
+    DevState s;
+    s.device = d;
+    if (cudaSetDevice(d) != cudaSuccess || cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking) != cudaSuccess) {
+      for (auto& o : c->devs) { cudaSetDevice(o.device); cudaStreamDestroy(o.stream); }
+      cudaSetDevice(prev);
+      delete c;
+      return MS_ERR_CUDA;
+    }
+    c->devs.push_back(s);
+  }
+  cudaSetDevice(prev);
+  *out = c;
+  return MS_OK;
+}
+
+int ms_destroy(ms_ctx* c) {
+  if (!c) return MS_ERR_ARG;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  for (auto& s : c->devs) {
+    cudaSetDevice(s.device);
+    if (s.stream) { cudaStreamSynchronize(s.stream); cudaStreamDestroy(s.stream); }
+    if (s.scratch) cudaFree(s.scratch);
+    for (auto& e3 : s.prof_pending) for (auto e : e3) cudaEventDestroy(e);
+    for (auto& e3 : s.prof_free) for (auto e : e3) cudaEventDestroy(e);
+    if (s.io) cudaFree(s.io);
+  }
+  cudaSetDevice(prev);
+  delete c;
+  return MS_OK;
+}
+
+const char* ms_last_error(ms_ctx* c) { return c ? c->err.c_str() : "null context"; }
+
+int ms_profile_read(ms_ctx* c, double* stream_ms, double* finalize_ms, int64_t* calls) {
+  if (!c) return MS_ERR_ARG;
+  double a = 0.0, b = 0.0;
+  int64_t n = 0;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  for (auto& s : c->devs) {
+    cudaSetDevice(s.device);
+    for (auto& e3 : s.prof_pending) {
+      float t01 = 0.f, t12 = 0.f;
+      if (cudaEventSynchronize(e3[2]) != cudaSuccess || cudaEventElapsedTime(&t01, e3[0], e3[1]) != cudaSuccess ||
+          cudaEventElapsedTime(&t12, e3[1], e3[2]) != cudaSuccess) {
+        cudaSetDevice(prev);
+        return fail(c, MS_ERR_CUDA, "ms_profile_read: event timing failed");
+      }
+      a += t01;
+      b += t12;
+      n++;
+      s.prof_free.push_back(e3);
+    }
+    s.prof_pending.clear();
+  }
+  cudaSetDevice(prev);
+  if (stream_ms) *stream_ms = a;
+  if (finalize_ms) *finalize_ms = b;
+  if (calls) *calls = n;
+  return MS_OK;
+}
+
+int ms_scratch_bytes(int64_t B, int64_t V, const ms_params* params, int64_t* out_bytes) {
+  if (!params || !out_bytes || B < 0 || V < 1) return MS_ERR_ARG;
+  const Plan P = make_plan(V, params, true);
+  *out_bytes = (int64_t)scratch_layout(B, V, P).total;
+  return MS_OK;
+}
+
+}  // extern "C"
+
+// Launch one [B, V] slice on device state s; every pointer is device memory.
+static int run_device(ms_ctx* ctx, DevState& s, const float* logits, int64_t B, int64_t V, int64_t ld,
+                      const int32_t* hist, const int64_t* hist_off, const ms_params* p, const double* u,
+                      int32_t* out_ids, const ms_diag* diag, cudaStream_t stream, bool profile) {
+  const Plan P = make_plan(V, p, hist != nullptr && hist_off != nullptr);
+  const ScratchLayout L = scratch_layout(B, V, P);
+  int rc = ensure(ctx, &s.scratch, &s.scratch_bytes, L.total);
+  if (rc) return rc;
+  char* base = (char*)s.scratch;
+  ms::Args A;
+  memset(&A, 0, sizeof A);
+  A.logits = logits;
+  A.ld = ld;
+  A.B = (int32_t)B;
+  A.V = (int32_t)V;
+  A.hist = hist;
+  A.hist_off = hist_off;
+  A.pen = p->repetition_penalty;
+  A.use_pen = P.use_pen;
+  A.mode = P.mode;
+  A.T = p->temperature;
+  A.temper = P.temper;
+  A.a = P.a;
+  A.k = P.k;
+  A.kw = P.kw;
+  A.use_topp = P.use_topp;
+  A.top_p = p->top_p;
+  A.u = u;
+  A.n_chunks = P.n_chunks;
+  A.stats = (ms::ChunkStat*)(base + L.stats);
+  A.cands = (ms::Cand*)(base + L.cands);
+  A.penbits = (P.use_pen && P.mode != ms::kGreedy) ? (uint32_t*)(base + L.penbits) : nullptr;
+  A.status = (int32_t*)(base + L.status);
+  s.status = A.status;
+  A.out_ids = out_ids;
+  if (diag) {
+    A.cand_cap = diag->cand_cap;
+    A.d_cand_ids = diag->cand_cap > 0 ? diag->cand_ids : nullptr;
+    A.d_cand_probs = diag->cand_cap > 0 ? diag->cand_probs : nullptr;
+    A.d_n_cand = diag->n_cand;
+    A.d_row_max = diag->row_max;
+    A.d_row_sum = diag->row_sum;
+    A.d_total = diag->total;
+    A.d_row_flags = diag->row_flags;
+  }
+  if (P.mode != ms::kGreedy && !u) return fail(ctx, MS_ERR_ARG, "ms_sample: sampled rows need u[B]");
+  MS_CUDA(ctx, cudaMemsetAsync(A.status, 0, sizeof(int32_t), stream));
+  cudaEvent_t* ev = nullptr;
+  if (profile) {
+    if (s.prof_free.empty()) {
+      std::array<cudaEvent_t, 3> e3;
+      for (auto& e : e3) MS_CUDA(ctx, cudaEventCreate(&e));
+      s.prof_free.push_back(e3);
+    }
+    s.prof_pending.push_back(s.prof_free.back());
+    s.prof_free.pop_back();
+    ev = s.prof_pending.back().data();
+  }
+  MS_CUDA(ctx, ms::launch_sample(A, stream, ev));
+  return MS_OK;
+}
+
+extern "C" int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V, int64_t ld,
+                         const int32_t* hist, const int64_t* hist_off, const ms_params* params,
+                         const double* u, int32_t* out_ids, ms_diag* diag, int flags, void* stream) {
+  if (!ctx) return MS_ERR_ARG;
+  if (!params) return fail(ctx, MS_ERR_ARG, "ms_sample: params is NULL");
+  if (B < 0) return fail(ctx, MS_ERR_ARG, "ms_sample: B < 0");
+  if (V < 1 || V > (int64_t)INT32_MAX / 2) return fail(ctx, MS_ERR_ARG, "ms_sample: V out of range");
+  if (ld < V) return fail(ctx, MS_ERR_ARG, "ms_sample: ld < V");
+  if (B == 0) return MS_OK;
+  if (!logits || !out_ids) return fail(ctx, MS_ERR_ARG, "ms_sample: logits/out_ids is NULL");
+  if (hist_off != nullptr && hist == nullptr)
+    return fail(ctx, MS_ERR_ARG, "ms_sample: hist_off given without hist");
+  if (hist_off == nullptr) hist = nullptr;
+  const bool host = (flags & MS_HOST_PTRS) != 0, dev = (flags & MS_DEVICE_PTRS) != 0;
+  if (host == dev) return fail(ctx, MS_ERR_ARG, "ms_sample: pass exactly one of MS_HOST_PTRS / MS_DEVICE_PTRS");
+  if (diag && diag->cand_cap < 0) return fail(ctx, MS_ERR_ARG, "ms_sample: diag->cand_cap < 0");
+  const ms_params pp = *params;
+  const bool greedy = !pp.do_sample || pp.temperature <= 0.0001;
+  if (!greedy && !u) return fail(ctx, MS_ERR_ARG, "ms_sample: sampled rows need u[B]");
+  int prev = 0;
+  cudaGetDevice(&prev);
+
+  if (dev) {
+    if (flags & MS_ROW_SHARDED) return fail(ctx, MS_ERR_ARG, "ms_sample: MS_ROW_SHARDED needs host pointers");
+    DevState& s = ctx->devs[0];
+    cudaSetDevice(s.device);
+    cudaStream_t st = stream ? (cudaStream_t)stream : s.stream;
+    int rc = run_device(ctx, s, logits, B, V, ld, hist, hist_off, &pp, u, out_ids, diag, st,
+                        (flags & MS_PROFILE) != 0);
+    if (rc == MS_OK && (flags & MS_SYNC)) {
+      cudaError_t e = cudaStreamSynchronize(st);
+      if (e != cudaSuccess) rc = fail(ctx, MS_ERR_CUDA, "ms_sample: %s", cudaGetErrorString(e));
+      if (rc == MS_OK) {
+        int32_t status = 0;
+        e = cudaMemcpy(&status, s.status, sizeof status, cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) rc = fail(ctx, MS_ERR_CUDA, "ms_sample: %s", cudaGetErrorString(e));
+        else if (status & ms::kStatusTimeout) rc = fail(ctx, MS_ERR_TIMEOUT, "ms_sample: a kernel wait timed out");
+      }
+    }
+    cudaSetDevice(prev);
+    return rc;
+  }
+
+  // ---- host pointers: stage through device memory, one row slice per device
+  if (hist_off) {
+    if (hist_off[0] < 0) return fail(ctx, MS_ERR_ARG, "ms_sample: hist_off[0] < 0");
+    for (int64_t r = 0; r < B; r++)
+      if (hist_off[r + 1] < hist_off[r]) return fail(ctx, MS_ERR_ARG, "ms_sample: hist_off not ascending");
+  }
+  const int nd = (flags & MS_ROW_SHARDED) ? (int)ctx->devs.size() : 1;
+  const int64_t per = (B + nd - 1) / nd;
+  int rc = MS_OK;
+  struct Slice { int64_t r0, rows; size_t o_logits, o_hist, o_off, o_u, o_out, o_cid, o_cp, o_nc, o_mx, o_sum, o_tot, o_fl; };
+  std::vector<Slice> slices(nd);
+  for (int d = 0; d < nd && rc == MS_OK; d++) {
+    DevState& s = ctx->devs[d];
+    Slice& sl = slices[d];
+    sl.r0 = d * per;
+    sl.rows = std::min<int64_t>(per, B - sl.r0);
+    if (sl.rows <= 0) { sl.rows = 0; continue; }
+    cudaSetDevice(s.device);
+    const int64_t h0 = hist_off ? hist_off[sl.r0] : 0;
+    const int64_t h1 = hist_off ? hist_off[sl.r0 + sl.rows] : 0;
+    const int64_t nh = h1 - h0;
+    size_t off = 0;
+    auto take = [&](size_t bytes) { size_t o = off; off = align_up(off + bytes, 256); return o; };
+    sl.o_logits = take((size_t)sl.rows * V * 4);
+    sl.o_hist = take((size_t)(nh > 0 ? nh : 1) * 4);
+    sl.o_off = take((size_t)(sl.rows + 1) * 8);
+    sl.o_u = take((size_t)sl.rows * 8);
+    sl.o_out = take((size_t)sl.rows * 4);
+    const int cap = diag ? diag->cand_cap : 0;
+    sl.o_cid = take((size_t)sl.rows * (cap > 0 ? cap : 1) * 4);
+    sl.o_cp = take((size_t)sl.rows * (cap > 0 ? cap : 1) * 4);
+    sl.o_nc = take((size_t)sl.rows * 4);
+    sl.o_mx = take((size_t)sl.rows * 8);
+    sl.o_sum = take((size_t)sl.rows * 8);
+    sl.o_tot = take((size_t)sl.rows * 8);
+    sl.o_fl = take((size_t)sl.rows * 4);
+    rc = ensure(ctx, &s.io, &s.io_bytes, off);
+    if (rc) break;
+    char* io = (char*)s.io;
+    cudaStream_t st = s.stream;
+    auto H2D = [&](size_t o, const void* src, size_t bytes) {
+      return cudaMemcpyAsync(io + o, src, bytes, cudaMemcpyHostToDevice, st);
+    };
+    cudaError_t e = cudaSuccess;
+    if (ld == V) e = H2D(sl.o_logits, logits + sl.r0 * ld, (size_t)sl.rows * V * 4);
+    else e = cudaMemcpy2DAsync(io + sl.o_logits, (size_t)V * 4, logits + sl.r0 * ld, (size_t)ld * 4,
+                               (size_t)V * 4, (size_t)sl.rows, cudaMemcpyHostToDevice, st);
+    const int32_t* dh = nullptr;
+    const int64_t* doff = nullptr;
+    if (e == cudaSuccess && hist_off) {
+      std::vector<int64_t> offs((size_t)sl.rows + 1);
+      for (int64_t r = 0; r <= sl.rows; r++) offs[r] = hist_off[sl.r0 + r] - h0;
+      if (nh > 0) e = H2D(sl.o_hist, hist + h0, (size_t)nh * 4);
+      if (e == cudaSuccess) e = cudaMemcpy(io + sl.o_off, offs.data(), offs.size() * 8, cudaMemcpyHostToDevice);
+      dh = (const int32_t*)(io + sl.o_hist);
+      doff = (const int64_t*)(io + sl.o_off);
+    }
+    if (e == cudaSuccess && u) e = H2D(sl.o_u, u + sl.r0, (size_t)sl.rows * 8);
+    if (e != cudaSuccess) { rc = fail(ctx, MS_ERR_CUDA, "ms_sample: H2D: %s", cudaGetErrorString(e)); break; }
+    ms_diag dd;
+    ms_diag* dp = nullptr;
+    if (diag) {
+      dd.cand_cap = diag->cand_cap;
+      dd.cand_ids = diag->cand_ids ? (int32_t*)(io + sl.o_cid) : nullptr;
+      dd.cand_probs = diag->cand_probs ? (float*)(io + sl.o_cp) : nullptr;
+      dd.n_cand = diag->n_cand ? (int32_t*)(io + sl.o_nc) : nullptr;
+      dd.row_max = diag->row_max ? (double*)(io + sl.o_mx) : nullptr;
+      dd.row_sum = diag->row_sum ? (double*)(io + sl.o_sum) : nullptr;
+      dd.total = diag->total ? (double*)(io + sl.o_tot) : nullptr;
+      dd.row_flags = diag->row_flags ? (int32_t*)(io + sl.o_fl) : nullptr;
+      dp = &dd;
+    }
+    rc = run_device(ctx, s, (const float*)(io + sl.o_logits), sl.rows, V, V, dh, doff, &pp,
+                    u ? (const double*)(io + sl.o_u) : nullptr, (int32_t*)(io + sl.o_out), dp, st,
+                    (flags & MS_PROFILE) != 0);
+    if (rc) break;
+    auto D2H = [&](void* dst, size_t o, size_t bytes) {
+      return cudaMemcpyAsync(dst, io + o, bytes, cudaMemcpyDeviceToHost, st);
+    };
+    e = D2H(out_ids + sl.r0, sl.o_out, (size_t)sl.rows * 4);
+    if (diag && e == cudaSuccess) {
+      const int cap = diag->cand_cap;
+      if (diag->cand_ids && cap > 0) e = D2H(diag->cand_ids + sl.r0 * cap, sl.o_cid, (size_t)sl.rows * cap * 4);
+      if (e == cudaSuccess && diag->cand_probs && cap > 0)
+        e = D2H(diag->cand_probs + sl.r0 * cap, sl.o_cp, (size_t)sl.rows * cap * 4);
+      if (e == cudaSuccess && diag->n_cand) e = D2H(diag->n_cand + sl.r0, sl.o_nc, (size_t)sl.rows * 4);
+      if (e == cudaSuccess && diag->row_max) e = D2H(diag->row_max + sl.r0, sl.o_mx, (size_t)sl.rows * 8);
+      if (e == cudaSuccess && diag->row_sum) e = D2H(diag->row_sum + sl.r0, sl.o_sum, (size_t)sl.rows * 8);
+      if (e == cudaSuccess && diag->total) e = D2H(diag->total + sl.r0, sl.o_tot, (size_t)sl.rows * 8);
+      if (e == cudaSuccess && diag->row_flags) e = D2H(diag->row_flags + sl.r0, sl.o_fl, (size_t)sl.rows * 4);
+    }
+    if (e != cudaSuccess) { rc = fail(ctx, MS_ERR_CUDA, "ms_sample: D2H: %s", cudaGetErrorString(e)); break; }
+  }
+  // wait for every device, then read each status word
+  for (int d = 0; d < nd; d++) {
+    if (slices[d].rows <= 0) continue;
+    DevState& s = ctx->devs[d];
+    cudaSetDevice(s.device);
+    cudaError_t e = cudaStreamSynchronize(s.stream);
+    if (e != cudaSuccess && rc == MS_OK) rc = fail(ctx, MS_ERR_CUDA, "ms_sample: %s", cudaGetErrorString(e));
+    if (rc == MS_OK) {
+      int32_t status = 0;
+      e = cudaMemcpy(&status, s.status, sizeof status, cudaMemcpyDeviceToHost);
+      if (e != cudaSuccess) rc = fail(ctx, MS_ERR_CUDA, "ms_sample: %s", cudaGetErrorString(e));
+      else if (status & ms::kStatusTimeout) rc = fail(ctx, MS_ERR_TIMEOUT, "ms_sample: a kernel wait timed out");
+    }
+  }
+  cudaSetDevice(prev);
+  return rc;
+}

@@ -1,0 +1,183 @@
+// Device helpers shared by the sampler kernels (sm_100a).
+//
+// Arithmetic contract (mini.js src/generation.js): JS computes in IEEE double
+// and rounds to fp32 on every Float32Array store.  The helpers below reproduce
+// those stores exactly where a value reaches the output:
+//   penalty      fp32(double(v) / p)  or fp32(double(v) * p)   (:22-23)
+//   temperature  fp32(double(x) / T)                           (:78)
+//   softmax term fp32(exp(double(x') - double(mx)))            (:14)
+//   probability  fp32(double(e) / sum)                         (:15)
+// CUDA's double `/` and `*` are IEEE round-to-nearest; __double2float_rn is the
+// fp32 store.  `exp` is CUDA's double exp (<= 1 ulp), so the fp32 term can
+// differ from V8's only when the double result sits next to an fp32 rounding
+// midpoint.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/minisample.h"
+
+namespace ms {
+
+constexpr int kThreads = 256;           // threads per CTA, every kernel
+constexpr int kChunk = 16384;           // logits per chunk CTA (64 KiB of smem)
+constexpr int kSub = 4;                 // bulk-copy pieces per chunk (16 KiB each)
+constexpr int kSubElems = kChunk / kSub;
+constexpr int kCap = 512;               // candidate slots per chunk
+constexpr int kKmax = 256;              // largest top_k on the candidate path
+constexpr int kNfMax = 4096;            // candidates the finalize CTA can rank
+constexpr int kKSum = 64;               // candidates kept for the sum correction when top_k is off
+
+// Status bits written by kernels (host maps them to MS_ERR_*).
+constexpr int kStatusTimeout = 0x1;
+
+struct ChunkStat {
+  float m;        // max of the penalised logits of the chunk (NaN ignored; -inf if none)
+  float tau;      // candidate threshold: at least top_k elements of the chunk are >= tau
+  double s;       // sum of fast exp2((x - m) * a) over the chunk (NaN if a NaN appeared)
+  int32_t n_cand; // elements >= tau (only the first kCap are stored)
+  int32_t best_i; // greedy: first index of the max (INT32_MAX if nothing > -inf)
+  float best_v;   // greedy: that max
+  int32_t pad;
+};
+
+struct Cand {
+  float x;        // penalised (untempered) logit
+  int32_t i;      // vocabulary id
+};
+
+enum Mode : int32_t { kGreedy = 0, kTopK = 1, kFull = 2 };
+
+struct Args {
+  const float* logits;
+  int64_t ld;
+  int32_t B, V;
+  const int32_t* hist;
+  const int64_t* hist_off;
+  double pen;            // repetition penalty (applied iff use_pen)
+  int32_t use_pen;
+  int32_t mode;
+  double T;              // temperature
+  int32_t temper;        // 1 when T != 1.0
+  float a;               // fp32(log2(e) / T): scale of the fast exp2 terms
+  int32_t k;             // top_k as the reference uses it (0 = off)
+  int32_t kw;            // per-warp rank of the thread maxima that bounds tau
+  int32_t use_topp;
+  double top_p;
+  const double* u;
+  int32_t n_chunks;
+  ChunkStat* stats;      // [B, n_chunks]
+  Cand* cands;           // [B, n_chunks, kCap]
+  uint32_t* penbits;     // [B, ceil(V/32)] penalty bitmap (slow path), may be null
+  int32_t* out_ids;      // [B]
+  int32_t* status;       // device status word
+  // diagnostics (each may be null)
+  int32_t cand_cap;
+  int32_t* d_cand_ids;
+  float* d_cand_probs;
+  int32_t* d_n_cand;
+  double* d_row_max;
+  double* d_row_sum;
+  double* d_total;
+  int32_t* d_row_flags;
+};
+
+// ---------------------------------------------------------------- exact helpers
+
+__device__ __forceinline__ float pen_apply(float v, double p) {
+  double d = (double)v;
+  return __double2float_rn(d > 0.0 ? __ddiv_rn(d, p) : __dmul_rn(d, p));
+}
+
+__device__ __forceinline__ float temper_exact(float x, double T, int temper) {
+  return temper ? __double2float_rn(__ddiv_rn((double)x, T)) : x;
+}
+
+__device__ __forceinline__ float term_exact(float xp, float mxp) {
+  return __double2float_rn(exp((double)xp - (double)mxp));
+}
+
+__device__ __forceinline__ float prob_exact(float e, double S) {
+  return __double2float_rn(__ddiv_rn((double)e, S));
+}
+
+// Fast fp32 softmax term relative to a reference max m: 2^((x - m) * a).  The
+// instruction sequence is fixed (no contraction) so the finalize kernel can
+// recompute a chunk's terms bit for bit.
+__device__ __forceinline__ float ex2_approx(float z) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(z));
+  return y;
+}
+__device__ __forceinline__ float term_fast(float x, float m, float a) {
+  return ex2_approx(__fmul_rn(__fsub_rn(x, m), a));
+}
+
+// ---------------------------------------------------------------- float keys
+// Order-preserving map of fp32 to uint32 (larger float -> larger key).
+__device__ __forceinline__ uint32_t fkey(float x) {
+  uint32_t b = __float_as_uint(x);
+  return b ^ ((uint32_t)((int32_t)b >> 31) | 0x80000000u);
+}
+__device__ __forceinline__ float fkey_inv(uint32_t k) {
+  uint32_t b = (k & 0x80000000u) ? (k ^ 0x80000000u) : ~k;
+  return __uint_as_float(b);
+}
+
+// ---------------------------------------------------------------- mbarrier / bulk copy
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+// Untiled TMA bulk copy global -> shared (no multicast).  dst, src 16-byte
+// aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+// Bounded wait on phase `parity`; false when ~`max_cycles` passed first.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long long max_cycles) {
+  uint32_t a = smem_addr(bar);
+  long long t0 = clock64();
+  for (;;) {
+    uint32_t done;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (clock64() - t0 > max_cycles) return false;
+  }
+}
+
+// ---------------------------------------------------------------- reductions
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ double warp_sum(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+}  // namespace ms

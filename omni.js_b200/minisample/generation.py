@@ -1,0 +1,146 @@
+"""Host mirror of mini.js's generation API (src/generation.js) on the CUDA sampler.
+
+Same names (snake_case), option normalisation, stopping rules and uniform-draw
+discipline as the reference, so a caller switching from the JS sampler finds
+the same behaviour:
+
+  normalize_options  src/generation.js:57-68  (`??` keeps 0 / False, defaults
+                     only None)
+  pick_token         src/generation.js:71-81  (penalty only once something was
+                     generated; one uniform per sampled step, none when greedy)
+  generate_tokens    src/generation.js:97-114 (onToken(id, n) returning False
+                     stops; EOS stops after it is appended)
+  generate_async     src/generation.js:121-142
+
+The backend is 'cuda' (libminisample).  Selecting it fails loudly when the
+library or a GPU is missing; there is no CPU fallback on this path.
+"""
+from __future__ import annotations
+
+import asyncio
+import random as _random
+
+import numpy as np
+
+from .sampler import SampleParams, Sampler
+
+_ACTIVE = None      # 'cuda' or None
+_SAMPLER = None
+
+
+def set_backend(name: str) -> str:
+    """Select the sampler backend; only 'cuda' lives here (src/tensor.js:15-20)."""
+    global _ACTIVE, _SAMPLER
+    if name != "cuda":
+        raise ValueError(f"[minisample] unknown backend: {name}")
+    if _SAMPLER is None:
+        _SAMPLER = Sampler()
+    _ACTIVE = "cuda"
+    return _ACTIVE
+
+
+def current_backend() -> str:
+    if _ACTIVE is None:
+        set_backend("cuda")
+    return _ACTIVE
+
+
+def _sampler() -> Sampler:
+    current_backend()
+    return _SAMPLER
+
+
+def _first(*vals, default):
+    for v in vals:
+        if v is not None:
+            return v
+    return default
+
+
+def normalize_options(options: dict | None) -> dict:
+    o = options or {}
+    return {
+        "max_new_tokens": _first(o.get("maxNewTokens"), o.get("max_new_tokens"), default=50),
+        "do_sample": _first(o.get("doSample"), o.get("do_sample"), default=True),
+        "temperature": _first(o.get("temperature"), default=1.0),
+        "top_k": _first(o.get("topK"), o.get("top_k"), default=50),
+        "top_p": _first(o.get("topP"), o.get("top_p"), default=0.95),
+        "repetition_penalty": _first(o.get("repetitionPenalty"), o.get("repetition_penalty"), default=1.0),
+        "eos_token_id": _first(o.get("eosTokenId"), o.get("eos_token_id"), default=None),
+        "on_token": o.get("onToken") or o.get("on_token") or None,
+    }
+
+
+def params_of(opts: dict) -> SampleParams:
+    return SampleParams(bool(opts["do_sample"]), float(opts["temperature"]), int(opts["top_k"]),
+                        float(opts["top_p"]), float(opts["repetition_penalty"]))
+
+
+def is_greedy(opts: dict) -> bool:
+    return (not opts["do_sample"]) or float(opts["temperature"]) <= 0.0001
+
+
+def pick_token(last_logits, generated, input_ids, opts, rand=_random.random):
+    """Next id from one row of logits; returns [id, True] like the reference."""
+    row = np.ascontiguousarray(np.asarray(last_logits, dtype=np.float32).reshape(1, -1))
+    hist = hist_off = None
+    if len(generated):
+        h = np.asarray(list(input_ids) + list(generated), dtype=np.int64)
+        # ids beyond int32 can never index the vocabulary: they are no-ops
+        h = np.where((h < 0) | (h > 2**31 - 1), -1, h).astype(np.int32)
+        hist = h
+        hist_off = np.array([0, h.shape[0]], dtype=np.int64)
+    u = None if is_greedy(opts) else np.array([rand()], dtype=np.float64)
+    ids = _sampler().sample(row, params_of(opts), u=u, hist=hist, hist_off=hist_off)
+    return [int(ids[0]), True]
+
+
+def last_token_logits(model, input_ids, cache):
+    """src/generation.js:83-90: the last row of model.forward(..., last_only=True)."""
+    logits = np.asarray(model.forward(input_ids, cache=cache, last_only=True), dtype=np.float32)
+    if logits.ndim == 2:
+        logits = logits[-1]
+    return logits
+
+
+def generate_tokens(model, input_ids, options=None, rand=_random.random):
+    opts = normalize_options(options)
+    cache = model.make_cache()
+    try:
+        generated = []
+        last = last_token_logits(model, input_ids, cache)
+        for step in range(int(opts["max_new_tokens"])):
+            next_id, _ = pick_token(last, generated, input_ids, opts, rand)
+            generated.append(next_id)
+            if opts["on_token"] and opts["on_token"](next_id, step + 1) is False:
+                break
+            if opts["eos_token_id"] is not None and next_id == opts["eos_token_id"]:
+                break
+            last = last_token_logits(model, [next_id], cache)
+        return generated
+    finally:
+        model.dispose_cache(cache)
+
+
+async def generate_async(model, input_ids, options=None, rand=_random.random):
+    opts = normalize_options(options)
+    tick = (options or {}).get("tick")
+    cache = model.make_cache()
+    try:
+        generated = []
+        last = last_token_logits(model, input_ids, cache)
+        for step in range(int(opts["max_new_tokens"])):
+            next_id, _ = pick_token(last, generated, input_ids, opts, rand)
+            generated.append(next_id)
+            if opts["on_token"] and opts["on_token"](next_id, step + 1) is False:
+                break
+            if opts["eos_token_id"] is not None and next_id == opts["eos_token_id"]:
+                break
+            if tick:
+                await tick()
+            else:
+                await asyncio.sleep(0)
+            last = last_token_logits(model, [next_id], cache)
+        return generated
+    finally:
+        model.dispose_cache(cache)
