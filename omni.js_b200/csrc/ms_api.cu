@@ -5,6 +5,7 @@
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <algorithm>
 #include <array>
 #include <vector>
 
@@ -20,11 +21,13 @@ namespace {
 struct DevState {
   int device = 0;
   cudaStream_t stream = nullptr;
-  void* scratch = nullptr;  // stats, candidates, penalty bitmap, status word
+  void* scratch = nullptr;  // stats, candidates, penalty bitmap
   size_t scratch_bytes = 0;
   void* io = nullptr;       // device copies of host arguments
   size_t io_bytes = 0;
-  int32_t* status = nullptr;  // status word of the last launch (inside scratch)
+  int32_t* status = nullptr;    // device status word (zeroed at creation and after a report)
+  int32_t* counters = nullptr;  // per-row chunk counters; kernels leave them at zero
+  int64_t counters_cap = 0;
   std::vector<std::array<cudaEvent_t, 3>> prof_pending;  // MS_PROFILE calls not yet read
   std::vector<std::array<cudaEvent_t, 3>> prof_free;
 };
@@ -60,15 +63,17 @@ Plan make_plan(int64_t V, const ms_params* p, bool have_hist) {
   } else {
     P.mode = ms::kFull;
   }
+  // every warp's kw-th largest thread maximum; kWarps * kw >= keff
+  const int warps = ms::kThreads / 32;
   const int keff = (P.mode == ms::kTopK) ? P.k : ms::kKSum;
-  P.kw = (keff + 7) / 8;
+  P.kw = (keff + warps - 1) / warps;
   if (P.kw < 1) P.kw = 1;
   if (P.kw > 32) P.kw = 32;
   return P;
 }
 
 struct ScratchLayout {
-  size_t stats = 0, cands = 0, penbits = 0, status = 0, total = 0;
+  size_t stats = 0, cands = 0, penbits = 0, total = 0;
 };
 
 ScratchLayout scratch_layout(int64_t B, int64_t V, const Plan& P) {
@@ -80,8 +85,6 @@ ScratchLayout scratch_layout(int64_t B, int64_t V, const Plan& P) {
   if (P.mode != ms::kGreedy) off = align_up(off + (size_t)B * P.n_chunks * ms::kCap * sizeof(ms::Cand), 256);
   L.penbits = off;
   if (P.use_pen && P.mode != ms::kGreedy) off = align_up(off + (size_t)B * ((V + 31) / 32) * 4, 256);
-  L.status = off;
-  off = align_up(off + 256, 256);
   L.total = off;
   return L;
 }
@@ -174,6 +177,8 @@ int ms_destroy(ms_ctx* c) {
     cudaSetDevice(s.device);
     if (s.stream) { cudaStreamSynchronize(s.stream); cudaStreamDestroy(s.stream); }
     if (s.scratch) cudaFree(s.scratch);
+    if (s.status) cudaFree(s.status);
+    if (s.counters) cudaFree(s.counters);
     for (auto& e3 : s.prof_pending) for (auto e : e3) cudaEventDestroy(e);
     for (auto& e3 : s.prof_free) for (auto e : e3) cudaEventDestroy(e);
     if (s.io) cudaFree(s.io);
@@ -217,7 +222,7 @@ int ms_profile_read(ms_ctx* c, double* stream_ms, double* finalize_ms, int64_t* 
 int ms_scratch_bytes(int64_t B, int64_t V, const ms_params* params, int64_t* out_bytes) {
   if (!params || !out_bytes || B < 0 || V < 1) return MS_ERR_ARG;
   const Plan P = make_plan(V, params, true);
-  *out_bytes = (int64_t)scratch_layout(B, V, P).total;
+  *out_bytes = (int64_t)scratch_layout(B, V, P).total + (int64_t)align_up((size_t)B * 4, 256) + 256;
   return MS_OK;
 }
 
@@ -231,6 +236,19 @@ static int run_device(ms_ctx* ctx, DevState& s, const float* logits, int64_t B, 
   const ScratchLayout L = scratch_layout(B, V, P);
   int rc = ensure(ctx, &s.scratch, &s.scratch_bytes, L.total);
   if (rc) return rc;
+  if (!s.status) {
+    MS_CUDA(ctx, cudaMalloc((void**)&s.status, 256));
+    MS_CUDA(ctx, cudaMemset(s.status, 0, 256));
+  }
+  if (s.counters_cap < B) {
+    if (s.counters) cudaFree(s.counters);
+    s.counters = nullptr;
+    s.counters_cap = 0;
+    const int64_t cap = B + B / 8 + 64;
+    MS_CUDA(ctx, cudaMalloc((void**)&s.counters, (size_t)cap * 4));
+    MS_CUDA(ctx, cudaMemset(s.counters, 0, (size_t)cap * 4));
+    s.counters_cap = cap;
+  }
   char* base = (char*)s.scratch;
   ms::Args A;
   memset(&A, 0, sizeof A);
@@ -241,6 +259,7 @@ static int run_device(ms_ctx* ctx, DevState& s, const float* logits, int64_t B, 
   A.hist = hist;
   A.hist_off = hist_off;
   A.pen = p->repetition_penalty;
+  A.rpen = 1.0 / p->repetition_penalty;
   A.use_pen = P.use_pen;
   A.mode = P.mode;
   A.T = p->temperature;
@@ -255,8 +274,9 @@ static int run_device(ms_ctx* ctx, DevState& s, const float* logits, int64_t B, 
   A.stats = (ms::ChunkStat*)(base + L.stats);
   A.cands = (ms::Cand*)(base + L.cands);
   A.penbits = (P.use_pen && P.mode != ms::kGreedy) ? (uint32_t*)(base + L.penbits) : nullptr;
-  A.status = (int32_t*)(base + L.status);
-  s.status = A.status;
+  A.status = s.status;
+  A.row_count = s.counters;
+  A.ksum = ms::kKSum;
   A.out_ids = out_ids;
   if (diag) {
     A.cand_cap = diag->cand_cap;
@@ -269,7 +289,6 @@ static int run_device(ms_ctx* ctx, DevState& s, const float* logits, int64_t B, 
     A.d_row_flags = diag->row_flags;
   }
   if (P.mode != ms::kGreedy && !u) return fail(ctx, MS_ERR_ARG, "ms_sample: sampled rows need u[B]");
-  MS_CUDA(ctx, cudaMemsetAsync(A.status, 0, sizeof(int32_t), stream));
   cudaEvent_t* ev = nullptr;
   if (profile) {
     if (s.prof_free.empty()) {
@@ -321,7 +340,10 @@ extern "C" int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V,
         int32_t status = 0;
         e = cudaMemcpy(&status, s.status, sizeof status, cudaMemcpyDeviceToHost);
         if (e != cudaSuccess) rc = fail(ctx, MS_ERR_CUDA, "ms_sample: %s", cudaGetErrorString(e));
-        else if (status & ms::kStatusTimeout) rc = fail(ctx, MS_ERR_TIMEOUT, "ms_sample: a kernel wait timed out");
+        else if (status & ms::kStatusTimeout) {
+          cudaMemset(s.status, 0, sizeof(int32_t));
+          rc = fail(ctx, MS_ERR_TIMEOUT, "ms_sample: a kernel wait timed out");
+        }
       }
     }
     cudaSetDevice(prev);
@@ -432,7 +454,10 @@ extern "C" int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V,
       int32_t status = 0;
       e = cudaMemcpy(&status, s.status, sizeof status, cudaMemcpyDeviceToHost);
       if (e != cudaSuccess) rc = fail(ctx, MS_ERR_CUDA, "ms_sample: %s", cudaGetErrorString(e));
-      else if (status & ms::kStatusTimeout) rc = fail(ctx, MS_ERR_TIMEOUT, "ms_sample: a kernel wait timed out");
+      else if (status & ms::kStatusTimeout) {
+        cudaMemset(s.status, 0, sizeof(int32_t));
+        rc = fail(ctx, MS_ERR_TIMEOUT, "ms_sample: a kernel wait timed out");
+      }
     }
   }
   cudaSetDevice(prev);

@@ -19,13 +19,14 @@
 
 namespace ms {
 
-constexpr int kThreads = 256;           // threads per CTA, every kernel
+constexpr int kThreads = 512;           // threads per CTA
 constexpr int kChunk = 16384;           // logits per chunk CTA (64 KiB of smem)
 constexpr int kSub = 4;                 // bulk-copy pieces per chunk (16 KiB each)
 constexpr int kSubElems = kChunk / kSub;
 constexpr int kCap = 512;               // candidate slots per chunk
 constexpr int kKmax = 256;              // largest top_k on the candidate path
-constexpr int kNfMax = 4096;            // candidates the finalize CTA can rank
+constexpr int kGathMax = 4096;          // candidates >= the row threshold the finalizer can hold
+constexpr int kFinMax = 1024;           // candidates the finalizer ranks exactly
 constexpr int kKSum = 64;               // candidates kept for the sum correction when top_k is off
 
 // Status bits written by kernels (host maps them to MS_ERR_*).
@@ -55,6 +56,7 @@ struct Args {
   const int32_t* hist;
   const int64_t* hist_off;
   double pen;            // repetition penalty (applied iff use_pen)
+  double rpen;           // fp64(1 / pen)
   int32_t use_pen;
   int32_t mode;
   double T;              // temperature
@@ -62,11 +64,13 @@ struct Args {
   float a;               // fp32(log2(e) / T): scale of the fast exp2 terms
   int32_t k;             // top_k as the reference uses it (0 = off)
   int32_t kw;            // per-warp rank of the thread maxima that bounds tau
+  int32_t ksum;          // candidates whose exact terms correct the fast sum (top_k or 64)
   int32_t use_topp;
   double top_p;
   const double* u;
   int32_t n_chunks;
   ChunkStat* stats;      // [B, n_chunks]
+  int32_t* row_count;    // [B] chunks finished per row (self-resetting)
   Cand* cands;           // [B, n_chunks, kCap]
   uint32_t* penbits;     // [B, ceil(V/32)] penalty bitmap (slow path), may be null
   int32_t* out_ids;      // [B]
@@ -87,6 +91,21 @@ struct Args {
 __device__ __forceinline__ float pen_apply(float v, double p) {
   double d = (double)v;
   return __double2float_rn(d > 0.0 ? __ddiv_rn(d, p) : __dmul_rn(d, p));
+}
+
+// pen_apply with the divide replaced by a multiply by rp = 1/p (rounded).
+// q = fp64(v * rp) is within 3 fp64 ulps of fp64(v / p), so both round to the
+// same fp32 unless q lies within a few ulps of an fp32 rounding midpoint (the
+// 29 mantissa bits an fp32 store drops read 1000...0); those rare cases, and
+// results in the fp32 subnormal range, take the exact divide.
+__device__ __forceinline__ float pen_apply_fast(float v, double p, double rp) {
+  const double d = (double)v;
+  if (!(d > 0.0)) return __double2float_rn(__dmul_rn(d, p));
+  const double q = __dmul_rn(d, rp);
+  const uint32_t low = (uint32_t)__double_as_longlong(q) & 0x1FFFFFFFu;
+  if ((uint32_t)(low - (0x10000000u - 16u)) <= 32u || q < 1.1754943508222875e-38)
+    return __double2float_rn(__ddiv_rn(d, p));
+  return __double2float_rn(q);
 }
 
 __device__ __forceinline__ float temper_exact(float x, double T, int temper) {

@@ -1,20 +1,27 @@
-// Sampler kernels for B200 (sm_100a).
+// Sampler kernel for B200 (sm_100a).
 //
-// One sampling step over a [B, V] fp32 logits block runs as two launches:
+// One sampling step over a [B, V] fp32 logits block is ONE launch of
+// sample_kernel, grid (ceil(V/16384), B), 512 threads, 64 KiB of shared memory
+// per CTA (3 CTAs per SM).  Each CTA owns one 16384-logit chunk of one row:
 //
-//   chunk_kernel    grid (ceil(V/16384), B).  A CTA stages one 64 KiB chunk of
-//                   one row in shared memory with TMA bulk copies, applies the
-//                   repetition penalty to it (src/generation.js:19-25), then
-//                   makes two passes over shared memory: (A) the chunk max and
-//                   a threshold tau that at least top_k chunk elements reach;
-//                   (B) a fast fp32 sum of 2^((x-m)*log2(e)/T) and the list of
-//                   elements >= tau.  Logits are read from HBM exactly once.
-//   finalize_kernel grid B.  A CTA merges its row's chunk results: the row
-//                   max, the softmax denominator (fast sum corrected with the
-//                   exact terms of every candidate), the exact fp32
-//                   probabilities of the candidates, their order
-//                   (prob desc, id asc), the top-k / top-p cut and the draw
-//                   (src/generation.js:9-17, 27-49).
+//   1. thread 0 starts four 16 KiB TMA bulk copies of the chunk into shared
+//      memory; meanwhile all threads turn the row's id history into a bitmap
+//      of the chunk's penalised ids (so repeated ids count once, the reference's
+//      Set, src/generation.js:20);
+//   2. the penalty is applied in shared memory to the flagged logits
+//      (src/generation.js:19-25);
+//   3. pass A: chunk max and a threshold tau that at least top_k elements of
+//      the chunk reach (from the sorted per-thread maxima of every warp);
+//   4. pass B: fast fp32 sum of 2^((x - m) * log2(e)/T) and the list of
+//      elements >= tau;
+//   5. the chunk results go to global scratch; the last CTA of the row to
+//      finish (atomic row counter) finalizes the row: softmax denominator
+//      (fast sum corrected with the exact terms of the top candidates), the
+//      exact fp32 probabilities of the candidates, their order
+//      (prob desc, id asc), top-k, top-p and the draw (src/generation.js:9-17,
+//      27-49).
+// Logits are read from HBM exactly once; everything after the load works on
+// shared memory or on the small candidate lists.
 //
 // Rows whose candidate set cannot be proven complete, and every row when top_k
 // is off (top_k <= 0 or >= V) or larger than 256, go through full_path: an
@@ -29,201 +36,9 @@ namespace ms {
 
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s: bound on every wait
 constexpr unsigned kAll = 0xffffffffu;
-
-// =============================================================== chunk kernel
-template <int MODE, bool PEN>
-__global__ void __launch_bounds__(kThreads, 3) chunk_kernel(const Args A) {
-  extern __shared__ __align__(128) unsigned char dyn_smem[];
-  float* tile = reinterpret_cast<float*>(dyn_smem);
-  __shared__ __align__(8) uint64_t bar[kSub];
-  __shared__ uint32_t penmask[kChunk / 32];
-  __shared__ Cand clist[kCap];
-  __shared__ int ccount;
-  __shared__ float w_max[kThreads / 32], w_tau[kThreads / 32];
-  __shared__ double w_sum[kThreads / 32];
-  __shared__ int w_bi[kThreads / 32];
-
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int c = blockIdx.x, r = blockIdx.y;
-  const int c0 = c * kChunk;
-  const int n = min(kChunk, A.V - c0);
-  const float* g = A.logits + (int64_t)r * A.ld + c0;
-  const bool bulk = ((reinterpret_cast<uintptr_t>(g) & 15) == 0) && ((n & 3) == 0);
-
-  if (tid == 0) {
-    ccount = 0;
-    if (bulk) {
-      for (int s = 0; s < kSub; s++) mbar_init(&bar[s], 1);
-      fence_mbar_init();
-    }
-  }
-  __syncthreads();
-  if (bulk) {
-    if (tid == 0) {
-      for (int s = 0; s < kSub; s++) {
-        const int b = s * kSubElems, cnt = min(kSubElems, n - b);
-        if (cnt > 0) {
-          mbar_expect_tx(&bar[s], (uint32_t)cnt * 4u);
-          bulk_g2s(tile + b, g + b, (uint32_t)cnt * 4u, &bar[s]);
-        }
-      }
-    }
-  } else {
-    for (int j = tid; j < n; j += kThreads) tile[j] = __ldg(g + j);
-  }
-  for (int j = n + tid; j < kChunk; j += kThreads) tile[j] = -INFINITY;
-  if (PEN)
-    for (int w = tid; w < kChunk / 32; w += kThreads) penmask[w] = 0u;
-  int timed_out = 0;
-  if (bulk) {
-    for (int s = 0; s < kSub; s++)
-      if (s * kSubElems < n && !mbar_wait(&bar[s], 0, kWaitCycles)) timed_out = 1;
-  }
-  if (__syncthreads_or(timed_out)) {
-    if (tid == 0) atomicOr(A.status, kStatusTimeout);
-    if (bulk)  // let any copy still in flight land before the CTA exits (bounded)
-      for (int s = 0; s < kSub; s++)
-        if (s * kSubElems < n) mbar_wait(&bar[s], 0, kWaitCycles);
-    return;
-  }
-
-  // ---- repetition penalty: each distinct in-range id once (Set semantics)
-  if (PEN) {
-    const int64_t h0 = A.hist_off[r], h1 = A.hist_off[r + 1];
-    for (int64_t h = h0 + tid; h < h1; h += kThreads) {
-      const int64_t j = (int64_t)A.hist[h] - c0;
-      if (j >= 0 && j < n) {
-        const uint32_t bit = 1u << (j & 31);
-        const uint32_t old = atomicOr(&penmask[j >> 5], bit);
-        if (!(old & bit)) tile[j] = pen_apply(tile[j], A.pen);
-      }
-    }
-    __syncthreads();
-  }
-
-  const float4* t4 = reinterpret_cast<const float4*>(tile);
-  constexpr int kIters = kChunk / 4 / kThreads;  // 16 float4 per thread
-
-  // ---- greedy: first index of the strict max (src/generation.js:51-55)
-  if (MODE == kGreedy) {
-    float bv = -INFINITY;
-    int bi = INT_MAX;
-#pragma unroll 4
-    for (int i = 0; i < kIters; i++) {
-      const int q = tid + i * kThreads;
-      const float4 v = t4[q];
-      const int j = c0 + 4 * q;
-      if (v.x > bv) { bv = v.x; bi = j; }
-      if (v.y > bv) { bv = v.y; bi = j + 1; }
-      if (v.z > bv) { bv = v.z; bi = j + 2; }
-      if (v.w > bv) { bv = v.w; bi = j + 3; }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(kAll, bv, o);
-      const int oi = __shfl_xor_sync(kAll, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-    }
-    if (lane == 0) { w_max[warp] = bv; w_bi[warp] = bi; }
-    __syncthreads();
-    if (tid == 0) {
-      for (int w = 1; w < kThreads / 32; w++)
-        if (w_max[w] > bv || (w_max[w] == bv && w_bi[w] < bi)) { bv = w_max[w]; bi = w_bi[w]; }
-      ChunkStat st;
-      st.m = bv; st.tau = bv; st.s = 0.0; st.n_cand = 0; st.best_i = bi; st.best_v = bv; st.pad = 0;
-      A.stats[(int64_t)r * A.n_chunks + c] = st;
-    }
-    return;
-  }
-
-  // ---- pass A: thread maxima -> chunk max and tau
-  float tm = -INFINITY;
-#pragma unroll 4
-  for (int i = 0; i < kIters; i++) {
-    const float4 v = t4[tid + i * kThreads];
-    tm = fmaxf(tm, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
-  }
-  // Warp bitonic sort of the 32 thread maxima (ascending).  At least kw of them
-  // are >= the warp's kw-th largest, so tau = min over warps of that value is
-  // reached by >= 8*kw >= top_k distinct elements of the chunk.
-  float sv = tm;
-#pragma unroll
-  for (int kk = 2; kk <= 32; kk <<= 1) {
-#pragma unroll
-    for (int jj = kk >> 1; jj > 0; jj >>= 1) {
-      const float o = __shfl_xor_sync(kAll, sv, jj);
-      const bool up = (lane & kk) == 0, lower = (lane & jj) == 0;
-      sv = (lower == up) ? fminf(sv, o) : fmaxf(sv, o);
-    }
-  }
-  const float wm = __shfl_sync(kAll, sv, 31);
-  const float wt = __shfl_sync(kAll, sv, 32 - A.kw);
-  if (lane == 0) { w_max[warp] = wm; w_tau[warp] = wt; }
-  __syncthreads();
-  float m = w_max[0], tau = w_tau[0];
-#pragma unroll
-  for (int w = 1; w < kThreads / 32; w++) { m = fmaxf(m, w_max[w]); tau = fminf(tau, w_tau[w]); }
-
-  // ---- pass B: fast exp sum (Kahan in fp32) and candidates >= tau
-  const float mref = (m == -INFINITY) ? 0.f : m;
-  const float a = A.a;
-  float s = 0.f, comp = 0.f;
-  const bool partial = n < kChunk;
-  const unsigned lt_mask = (1u << lane) - 1u;
-  auto append = [&](bool pred, float x, int idx) {
-    const unsigned msk = __ballot_sync(kAll, pred);
-    if (msk) {
-      const int leader = __ffs(msk) - 1;
-      int base = 0;
-      if (lane == leader) base = atomicAdd(&ccount, __popc(msk));
-      base = __shfl_sync(kAll, base, leader);
-      if (pred) {
-        const int pos = base + __popc(msk & lt_mask);
-        if (pos < kCap) clist[pos] = Cand{x, idx};
-      }
-    }
-  };
-#pragma unroll 2
-  for (int i = 0; i < kIters; i++) {
-    const int q = tid + i * kThreads;
-    const float4 v = t4[q];
-    const int j = 4 * q;
-    float e0 = term_fast(v.x, mref, a), e1 = term_fast(v.y, mref, a);
-    float e2 = term_fast(v.z, mref, a), e3 = term_fast(v.w, mref, a);
-    if (partial) {
-      if (j >= n) e0 = 0.f;
-      if (j + 1 >= n) e1 = 0.f;
-      if (j + 2 >= n) e2 = 0.f;
-      if (j + 3 >= n) e3 = 0.f;
-    }
-    const float t = __fadd_rn(__fadd_rn(e0, e1), __fadd_rn(e2, e3));
-    const float y = __fsub_rn(t, comp);
-    const float ss = __fadd_rn(s, y);
-    comp = __fsub_rn(__fsub_rn(ss, s), y);
-    s = ss;
-    const bool p0 = v.x >= tau, p1 = v.y >= tau, p2 = v.z >= tau, p3 = v.w >= tau;
-    if (__any_sync(kAll, p0 || p1 || p2 || p3)) {
-      append(p0 && j < n, v.x, c0 + j);
-      append(p1 && j + 1 < n, v.y, c0 + j + 1);
-      append(p2 && j + 2 < n, v.z, c0 + j + 2);
-      append(p3 && j + 3 < n, v.w, c0 + j + 3);
-    }
-  }
-  double ds = (double)s - (double)comp;
-  ds = warp_sum(ds);
-  if (lane == 0) w_sum[warp] = ds;
-  __syncthreads();
-  const int nc = min(ccount, kCap);
-  Cand* dst = A.cands + ((int64_t)r * A.n_chunks + c) * kCap;
-  for (int j = tid; j < nc; j += kThreads) dst[j] = clist[j];
-  if (tid == 0) {
-    double S = 0.0;
-    for (int w = 0; w < kThreads / 32; w++) S += w_sum[w];
-    ChunkStat st;
-    st.m = m; st.tau = tau; st.s = S; st.n_cand = ccount; st.best_i = INT_MAX; st.best_v = m; st.pad = 0;
-    A.stats[(int64_t)r * A.n_chunks + c] = st;
-  }
-}
+constexpr int kWarps = kThreads / 32;
+constexpr int kWarpCap = 32;  // candidate queue slots per warp and chunk
+constexpr int kFinChunks = 256;  // chunks whose scale the finalizer caches
 
 // =============================================================== full-row path
 struct RowInfo {
@@ -245,12 +60,15 @@ struct SelShared {
   double mass[256];
   double above;
   uint32_t prefix;
-  double total_w;      // weight of all non-NaN elements (first round)
-  int red_i[kThreads / 32];
-  int red_i2[kThreads / 32];
-  double red_d[kThreads / 32];
+  int digit, rem;
+  double total_w;
+  int red_i[kWarps];
+  int red_i2[kWarps];
+  double red_d[kWarps];
   unsigned long long pre[kThreads];
   int result;
+  float lohi[2];
+  float pstar;
 };
 
 __device__ __forceinline__ float load_x(const RowInfo& R, int i) {
@@ -268,9 +86,8 @@ __device__ __forceinline__ float prob_of(const RowInfo& R, float x) {
 // Value v of the row such that W(x > v) < target <= W(x >= v), where W counts
 // elements (by_mass false) or sums their fast probability mass.  Only
 // non-empty buckets qualify; a target above the total selects the smallest
-// element.  *above_out = W(x > v).
-__device__ float radix_select(const RowInfo& R, bool by_mass, double target, SelShared& sh,
-                              double* above_out) {
+// element.
+__device__ float radix_select(const RowInfo& R, bool by_mass, double target, SelShared& sh) {
   const int tid = threadIdx.x;
   uint32_t prefix = 0, pmask = 0;
   double above = 0.0;
@@ -291,9 +108,6 @@ __device__ float radix_select(const RowInfo& R, bool by_mass, double target, Sel
     if (tid == 0) {
       double cum = above;
       int chosen = -1, last = -1;
-      double tot = 0.0;
-      for (int d = 255; d >= 0; d--) tot += by_mass ? sh.mass[d] : (double)sh.cnt[d];
-      if (shift == 24) sh.total_w = tot;
       for (int d = 255; d >= 0; d--) {
         if (sh.cnt[d] == 0) continue;
         last = d;
@@ -314,18 +128,16 @@ __device__ float radix_select(const RowInfo& R, bool by_mass, double target, Sel
     pmask |= 0xFFu << shift;
     __syncthreads();
   }
-  *above_out = above;
   return fkey_inv(prefix);
 }
 
 // Keys [lo, hi] with pred(lo) true and pred monotone (true, then false as the
-// key grows): returns the largest key with pred true.  Warp 0 evaluates 32
+// key grows): returns the largest key with pred true.  One warp evaluates 32
 // probes per round.  `dir` -1 searches downward (pred true at hi, returns the
 // smallest key with pred true).
 template <typename Pred>
 __device__ uint32_t warp_boundary_search(uint32_t lo, uint32_t hi, int dir, Pred pred) {
   const int lane = threadIdx.x & 31;
-  // map so that we always search "largest true" over [0, span]
   const uint64_t base = dir > 0 ? lo : hi;
   uint64_t L = 0, H = (uint64_t)hi - lo;
   while (H > L) {
@@ -335,12 +147,11 @@ __device__ uint32_t warp_boundary_search(uint32_t lo, uint32_t hi, int dir, Pred
     const uint32_t key = dir > 0 ? (uint32_t)(base + p) : (uint32_t)(base - p);
     const bool t = pred(key);
     const unsigned msk = __ballot_sync(kAll, t);
-    // msk is a prefix of lanes (monotone predicate)
     const int ntrue = __popc(msk);
     const uint64_t p_last = __shfl_sync(kAll, p, ntrue > 0 ? ntrue - 1 : 0);
     const uint64_t p_next = __shfl_sync(kAll, p, ntrue < 32 ? ntrue : 31);
     if (ntrue == 0) {
-      H = p_next - 1;  // p_next is lane 0's probe here
+      H = p_next - 1;
     } else {
       L = p_last;
       if (ntrue < 32) H = p_next - 1;
@@ -350,13 +161,27 @@ __device__ uint32_t warp_boundary_search(uint32_t lo, uint32_t hi, int dir, Pred
   return dir > 0 ? (uint32_t)(base + L) : (uint32_t)(base - L);
 }
 
+// Smallest / largest x (fp32) with prob_of(x) == prob_of(v), searched by one
+// full warp of the caller; v itself qualifies.
+__device__ float tie_low(const RowInfo& R, float v) {
+  const float pv = prob_of(R, v);
+  const uint32_t kv = fkey(v);
+  const uint32_t kNegInf = fkey(-INFINITY);
+  auto same = [&](uint32_t key) { return prob_of(R, fkey_inv(key)) == pv; };
+  return fkey_inv(warp_boundary_search(kNegInf <= kv ? kNegInf : kv, kv, -1, same));
+}
+__device__ float tie_high(const RowInfo& R, float v) {
+  const float pv = prob_of(R, v);
+  const uint32_t kv = fkey(v);
+  const uint32_t kM = fkey(R.M) > kv ? fkey(R.M) : kv;
+  auto same = [&](uint32_t key) { return prob_of(R, fkey_inv(key)) == pv; };
+  return fkey_inv(warp_boundary_search(kv, kM, +1, same));
+}
+
 struct GroupSel {
   int index;       // vocabulary id of the selected element
   int64_t rank;    // 1-based position in (prob desc, id asc) order
   double cum;      // fast cumulative mass through it
-  double mass_hi;  // fast mass strictly above its tie group
-  int64_t cnt_hi;  // elements strictly above its tie group
-  float p;         // its exact probability
 };
 
 // Resolve the tie group of v (all x with prob_of(x) == prob_of(v)), then the
@@ -364,21 +189,12 @@ struct GroupSel {
 __device__ GroupSel resolve_group(const RowInfo& R, float v, bool by_mass, double target,
                                   SelShared& sh) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  __shared__ float s_lohi[2];
-  __shared__ float s_p;
   if (warp == 0) {
-    const float pv = prob_of(R, v);
-    const uint32_t kv = fkey(v);
-    const uint32_t kM = fkey(R.M) > kv ? fkey(R.M) : kv;
-    const uint32_t kNegInf = fkey(-INFINITY);
-    auto same = [&](uint32_t key) { return prob_of(R, fkey_inv(key)) == pv; };
-    const uint32_t khi = warp_boundary_search(kv, kM, +1, same);
-    const uint32_t klo = warp_boundary_search(kNegInf <= kv ? kNegInf : kv, kv, -1, same);
-    if (lane == 0) { s_lohi[0] = fkey_inv(klo); s_lohi[1] = fkey_inv(khi); s_p = pv; }
+    const float lo = tie_low(R, v), hi = tie_high(R, v);
+    if (lane == 0) { sh.lohi[0] = lo; sh.lohi[1] = hi; sh.pstar = prob_of(R, v); }
   }
   __syncthreads();
-  const float xlo = s_lohi[0], xhi = s_lohi[1], pstar = s_p;
-  // counts above / inside the group, fast mass above
+  const float xlo = sh.lohi[0], xhi = sh.lohi[1], pstar = sh.pstar;
   int c_hi = 0, c_g = 0;
   double m_hi = 0.0;
   for (int i = tid; i < R.V; i += kThreads) {
@@ -393,7 +209,7 @@ __device__ GroupSel resolve_group(const RowInfo& R, float v, bool by_mass, doubl
   __syncthreads();
   int64_t CH = 0, CG = 0;
   double MH = 0.0;
-  for (int w = 0; w < kThreads / 32; w++) { CH += sh.red_i[w]; CG += sh.red_i2[w]; MH += sh.red_d[w]; }
+  for (int w = 0; w < kWarps; w++) { CH += sh.red_i[w]; CG += sh.red_i2[w]; MH += sh.red_d[w]; }
   __syncthreads();
   int64_t j;
   if (by_mass) {
@@ -435,26 +251,21 @@ __device__ GroupSel resolve_group(const RowInfo& R, float v, bool by_mass, doubl
   gsel.index = sh.result < 0 ? 0 : sh.result;
   gsel.rank = CH + j;
   gsel.cum = MH + (double)j * (double)pstar;
-  gsel.mass_hi = MH;
-  gsel.cnt_hi = CH;
-  gsel.p = pstar;
   __syncthreads();
   return gsel;
 }
 
 __device__ GroupSel select_rank(const RowInfo& R, int64_t k, SelShared& sh) {
-  double above;
-  const float v = radix_select(R, false, (double)k, sh, &above);
+  const float v = radix_select(R, false, (double)k, sh);
   return resolve_group(R, v, false, (double)k, sh);
 }
 __device__ GroupSel select_mass(const RowInfo& R, double target, SelShared& sh) {
-  double above;
-  const float v = radix_select(R, true, target, sh, &above);
+  const float v = radix_select(R, true, target, sh);
   return resolve_group(R, v, true, target, sh);
 }
 
 // Exact top-k / top-p / draw over the whole row (src/generation.js:27-49).
-__device__ void full_path(const Args& A, int r, const RowInfo& R, SelShared& sh, int flags) {
+__device__ __noinline__ void full_path(const Args& A, int r, const RowInfo& R, SelShared& sh, int flags) {
   const int tid = threadIdx.x;
   const int V = R.V;
   const bool use_k = A.k > 0 && A.k < V;
@@ -476,7 +287,7 @@ __device__ void full_path(const Args& A, int r, const RowInfo& R, SelShared& sh,
     if ((tid & 31) == 0) sh.red_d[tid >> 5] = t;
     __syncthreads();
     mass_n = 0.0;
-    for (int w = 0; w < kThreads / 32; w++) mass_n += sh.red_d[w];
+    for (int w = 0; w < kWarps; w++) mass_n += sh.red_d[w];
     __syncthreads();
     n = V;
     last_id = -1;
@@ -490,10 +301,7 @@ __device__ void full_path(const Args& A, int r, const RowInfo& R, SelShared& sh,
       last_id = gp.index;
     }
   }
-  if (last_id < 0) {
-    const GroupSel gl = select_rank(R, n, sh);
-    last_id = gl.index;
-  }
+  if (last_id < 0) last_id = select_rank(R, n, sh).index;
   const double u = A.u ? A.u[r] : 0.0;
   const double rr = u * total;
   int id;
@@ -511,17 +319,17 @@ __device__ void full_path(const Args& A, int r, const RowInfo& R, SelShared& sh,
   }
 }
 
-// =============================================================== finalize kernel
-struct FinShared {
-  unsigned long long keys[kNfMax];
+// =============================================================== finalize
+struct FinSmem {
+  Cand gath[kGathMax];
+  unsigned long long keys[kFinMax];
   SelShared sel;
-  int nf;
-  int slow;
+  int nf, nF, slow, nan_row, overflow;
   unsigned long long corr;  // fixed-point (2^-50) sum of the candidate corrections
-  double S;
-  float M, Mp, tau_row;
-  int nan_row, overflow;
-  double scale0;
+  double S, S_fast, scale0;
+  float M, Mp, tau_row, xk, xlo;
+  float cm[kFinChunks];      // chunk maxima (first kFinChunks chunks)
+  double cs[kFinChunks];     // chunk_scale of each
 };
 
 __device__ __forceinline__ double chunk_scale(const Args& A, float mc, float Mp) {
@@ -529,106 +337,302 @@ __device__ __forceinline__ double chunk_scale(const Args& A, float mc, float Mp)
   return (mc == -INFINITY) ? 0.0 : exp((double)mc / A.T - (double)Mp);
 }
 
-template <int MODE>
-__global__ void __launch_bounds__(kThreads) finalize_kernel(const Args A) {
-  extern __shared__ __align__(16) unsigned char fin_smem[];
-  FinShared& sh = *reinterpret_cast<FinShared*>(fin_smem);
+// k-th largest x (1 <= k <= n) of the gathered candidates: radix select on
+// order-preserving keys, 8 bits per round.
+__device__ float kth_largest(const Cand* g, int n, int k, SelShared& sh) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int r = blockIdx.x;
+  uint32_t prefix = 0, pmask = 0;
+  int rem = k;
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int d = tid; d < 256; d += kThreads) sh.cnt[d] = 0;
+    __syncthreads();
+    for (int j = tid; j < n; j += kThreads) {
+      const uint32_t key = fkey(g[j].x);
+      if ((key & pmask) == prefix) atomicAdd(&sh.cnt[(key >> shift) & 255], 1);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // lane l holds digits 255-8l .. 248-8l (descending)
+      int c[8], s = 0;
+#pragma unroll
+      for (int i = 0; i < 8; i++) { c[i] = sh.cnt[255 - 8 * lane - i]; s += c[i]; }
+      int incl = s;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t = __shfl_up_sync(kAll, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const int excl = incl - s;
+      if (excl < rem && incl >= rem) {
+        int run = excl;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          if (run + c[i] >= rem) { sh.digit = 255 - 8 * lane - i; sh.rem = rem - run; break; }
+          run += c[i];
+        }
+      }
+    }
+    __syncthreads();
+    prefix |= (uint32_t)sh.digit << shift;
+    pmask |= 0xFFu << shift;
+    rem = sh.rem;
+    __syncthreads();
+  }
+  return fkey_inv(prefix);
+}
+
+__device__ __forceinline__ double key_prob(unsigned long long key) {
+  return (double)__uint_as_float(0xFFFFFFFFu - (uint32_t)(key >> 32));
+}
+
+// Top-k, top-p and the draw over the first A.k sorted candidates
+// (src/generation.js:32-48), called by one full warp.  The reference sums in
+// fp64 sequentially.  When every probability is >= 2^-30 (a multiple of
+// 2^-53) and the k probabilities sum below 1, every partial sum is exact, so
+// the warp-parallel prefix sums, the cut and the draw equal the sequential
+// ones bit for bit; otherwise lane 0 runs the sequential loops.
+__device__ void topk_draw(const Args& A, int r, const unsigned long long* sorted, float Mp, double S,
+                          int* n_out) {
+  const int lane = threadIdx.x & 31;
+  const int k = A.k;
+  const int per = (k + 31) / 32;
+  const int i0 = min(k, lane * per), i1 = min(k, i0 + per);
+  double ls = 0.0;
+  bool ok = true;
+  for (int i = i0; i < i1; i++) {
+    const double p = key_prob(sorted[i]);
+    ok &= p >= 9.313225746154785e-10;  // 2^-30
+    ls += p;
+  }
+  double incl = ls;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double t = __shfl_up_sync(kAll, incl, o);
+    if (lane >= o) incl += t;
+  }
+  const double total_k = __shfl_sync(kAll, incl, 31);
+  const bool exact = __all_sync(kAll, ok) && total_k < 1.0;
+  const double u = A.u ? A.u[r] : 0.0;
+  int n = k, id = 0;
+  double total = 0.0;
+  if (exact) {
+    // first i with prefix_i >= target, or k when none
+    auto first_reach = [&](double target, int limit) {
+      double acc = incl - ls;
+      int hit = INT_MAX;
+      for (int i = i0; i < min(i1, limit); i++) {
+        acc += key_prob(sorted[i]);
+        if (acc >= target) { hit = i; break; }
+      }
+      return __reduce_min_sync(kAll, (unsigned)hit);
+    };
+    if (A.use_topp) {
+      const unsigned h = first_reach(A.top_p, k);
+      n = (h == (unsigned)INT_MAX) ? k : (int)h + 1;
+    }
+    // total = prefix_{n-1}, held by the lane owning n-1
+    double acc = incl - ls, tot = 0.0;
+    for (int i = i0; i < i1; i++) {
+      acc += key_prob(sorted[i]);
+      if (i == n - 1) tot = acc;
+    }
+    const int owner = (n - 1) / per;
+    total = __shfl_sync(kAll, tot, owner);
+    const double rr = u * total;
+    const unsigned h = first_reach(rr, n);
+    id = (int)(uint32_t)sorted[h == (unsigned)INT_MAX ? n - 1 : h];
+  } else if (lane == 0) {
+    if (A.use_topp) {
+      double a2 = 0.0;
+      int cut = n;
+      for (int i = 0; i < n; i++) {
+        a2 += key_prob(sorted[i]);
+        if (a2 >= A.top_p) { cut = i + 1; break; }
+      }
+      n = cut > 1 ? cut : 1;
+    }
+    for (int i = 0; i < n; i++) total += key_prob(sorted[i]);
+    double rr = u * total;
+    id = (int)(uint32_t)sorted[n - 1];
+    for (int i = 0; i < n; i++) {
+      rr -= key_prob(sorted[i]);
+      if (rr <= 0.0) { id = (int)(uint32_t)sorted[i]; break; }
+    }
+  }
+  if (lane == 0) {
+    A.out_ids[r] = id;
+    if (A.d_n_cand) A.d_n_cand[r] = n;
+    if (A.d_total) A.d_total[r] = total;
+    if (A.d_row_max) A.d_row_max[r] = (double)Mp;
+    if (A.d_row_sum) A.d_row_sum[r] = S;
+    if (A.d_row_flags) A.d_row_flags[r] = 0;
+    *n_out = n;
+  }
+}
+
+template <int MODE>
+__device__ __noinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const ChunkStat* st = A.stats + (int64_t)r * A.n_chunks;
+  const int V = A.V;
 
   if (MODE == kGreedy) {
-    if (tid == 0) {
+    if (warp == 0) {
       float bv = -INFINITY;
       int bi = INT_MAX;
-      for (int c = 0; c < A.n_chunks; c++) {
-        const ChunkStat s = st[c];
-        if (s.best_v > bv || (s.best_v == bv && s.best_i < bi)) { bv = s.best_v; bi = s.best_i; }
+      for (int c = lane; c < A.n_chunks; c += 32) {
+        const float v = __ldcg(&st[c].best_v);
+        const int i = __ldcg(&st[c].best_i);
+        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
       }
-      const float x0 = A.logits[(int64_t)r * A.ld];
-      const int id = (x0 != x0 || bv == -INFINITY || bi == INT_MAX) ? 0 : bi;
-      A.out_ids[r] = id;
-      if (A.d_row_flags) A.d_row_flags[r] = MS_ROW_GREEDY;
-      if (A.d_n_cand) A.d_n_cand[r] = 0;
-      if (A.d_row_max) A.d_row_max[r] = (double)bv;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(kAll, bv, o);
+        const int oi = __shfl_xor_sync(kAll, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      if (lane == 0) {
+        // src/generation.js:51-55: a NaN at index 0 is never beaten
+        const float x0 = A.logits[(int64_t)r * A.ld];
+        const int id = (x0 != x0 || bv == -INFINITY || bi == INT_MAX) ? 0 : bi;
+        A.out_ids[r] = id;
+        if (A.d_row_flags) A.d_row_flags[r] = MS_ROW_GREEDY;
+        if (A.d_n_cand) A.d_n_cand[r] = 0;
+        if (A.d_row_max) A.d_row_max[r] = (double)bv;
+      }
     }
     return;
   }
 
-  // ---- row max, NaN detection, overflow, tau_row
-  if (tid == 0) {
+  // ---- row max, NaN detection, overflow, tau_row, fast sum
+  if (warp == 0) {
     float M = -INFINITY, tr = -INFINITY;
     int nanr = 0, ovf = 0;
-    for (int c = 0; c < A.n_chunks; c++) {
-      const ChunkStat s = st[c];
-      M = fmaxf(M, s.m);
-      tr = fmaxf(tr, s.tau);
-      if (s.s != s.s) nanr = 1;
-      if (s.n_cand > kCap) ovf = 1;
+    for (int c = lane; c < A.n_chunks; c += 32) {
+      const float m = __ldcg(&st[c].m), t = __ldcg(&st[c].tau);
+      const double s = __ldcg(&st[c].s);
+      M = fmaxf(M, m);
+      tr = fmaxf(tr, t);
+      nanr |= (s != s);
+      ovf |= (__ldcg(&st[c].n_cand) > kCap);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      M = fmaxf(M, __shfl_xor_sync(kAll, M, o));
+      tr = fmaxf(tr, __shfl_xor_sync(kAll, tr, o));
+      nanr |= __shfl_xor_sync(kAll, nanr, o);
+      ovf |= __shfl_xor_sync(kAll, ovf, o);
     }
     const float Mp = temper_exact(M, A.T, A.temper);
     if (M == -INFINITY || isinf(Mp) || Mp != Mp) nanr = 1;
-    sh.M = M; sh.Mp = Mp; sh.tau_row = tr; sh.nan_row = nanr; sh.overflow = ovf;
-    sh.nf = 0; sh.slow = ovf; sh.corr = 0ull;
+    double S = 0.0;
     if (!nanr) {
-      double S = 0.0;
-      for (int c = 0; c < A.n_chunks; c++) {
-        const ChunkStat s = st[c];
-        if (s.m != -INFINITY) S += s.s * chunk_scale(A, s.m, Mp);
+      for (int c = lane; c < A.n_chunks; c += 32) {
+        const float m = __ldcg(&st[c].m);
+        const double sc = chunk_scale(A, m, Mp);
+        if (m != -INFINITY) S += __ldcg(&st[c].s) * sc;
+        if (c < kFinChunks) { F.cm[c] = m; F.cs[c] = sc; }
       }
-      sh.S = S;
-      sh.scale0 = exp((double)M / A.T - (double)Mp);
+      S = warp_sum(S);
+    }
+    if (lane == 0) {
+      F.M = M; F.Mp = Mp; F.tau_row = tr; F.nan_row = nanr; F.overflow = ovf;
+      F.nf = 0; F.slow = ovf; F.corr = 0ull; F.S_fast = S;
+      F.scale0 = nanr ? 0.0 : exp((double)M / A.T - (double)Mp);
     }
   }
   __syncthreads();
-  const int V = A.V;
-  if (sh.nan_row) {
+  if (F.nan_row) {
     // softmax is NaN everywhere: the stable sort keeps id order, no acc reaches
     // topP, r is NaN, and the draw loop falls through to the last candidate.
     if (tid == 0) {
       const bool use_k = A.k > 0 && A.k < V;
       A.out_ids[r] = use_k ? A.k - 1 : V - 1;
       if (A.d_n_cand) A.d_n_cand[r] = use_k ? A.k : V;
-      if (A.d_row_max) A.d_row_max[r] = (double)sh.Mp;
+      if (A.d_row_max) A.d_row_max[r] = (double)F.Mp;
       if (A.d_row_sum) A.d_row_sum[r] = __longlong_as_double(0x7ff8000000000000ll);
       if (A.d_total) A.d_total[r] = __longlong_as_double(0x7ff8000000000000ll);
       if (A.d_row_flags) A.d_row_flags[r] = MS_ROW_NAN;
     }
     return;
   }
-  const float M = sh.M, Mp = sh.Mp, tau_row = sh.tau_row;
+  const float M = F.M, Mp = F.Mp, tau_row = F.tau_row;
 
-  // ---- gather candidates >= tau_row (complete unless a chunk overflowed)
-  Cand* gath = reinterpret_cast<Cand*>(sh.keys);
-  for (int c = 0; c < A.n_chunks; c++) {
-    const int nc = min(st[c].n_cand, kCap);
+  // ---- gather the candidates >= tau_row (all of them unless a chunk overflowed)
+  for (int c = warp; c < A.n_chunks; c += kWarps) {  // one chunk per warp at a time
+    const int nc = min(__ldcg(&st[c].n_cand), kCap);
     const Cand* src = A.cands + ((int64_t)r * A.n_chunks + c) * kCap;
-    for (int j = tid; j < nc; j += kThreads) {
-      const Cand cd = src[j];
-      if (cd.x >= tau_row) {
-        const int pos = atomicAdd(&sh.nf, 1);
-        if (pos < kNfMax) gath[pos] = cd;
+    for (int j0 = 0; j0 < nc; j0 += 32) {
+      const int j = j0 + lane;
+      Cand cd;
+      cd.x = -INFINITY;
+      cd.i = 0;
+      if (j < nc) {
+        const float2 v = __ldcg(reinterpret_cast<const float2*>(src + j));
+        cd.x = v.x;
+        cd.i = __float_as_int(v.y);
+      }
+      const bool keep = j < nc && cd.x >= tau_row;
+      const unsigned msk = __ballot_sync(kAll, keep);
+      if (msk) {
+        int base = 0;
+        if (lane == 0) base = atomicAdd(&F.nf, __popc(msk));
+        base = __shfl_sync(kAll, base, 0);
+        const int pos = base + __popc(msk & ((1u << lane) - 1u));
+        if (keep && pos < kGathMax) F.gath[pos] = cd;
       }
     }
   }
   __syncthreads();
-  const int nf = sh.nf;
-  if (nf > kNfMax) { if (tid == 0) sh.slow = 1; }
-  // ---- exact terms of the candidates; correct the fast sum with them
-  const int nfc = min(nf, kNfMax);
-  for (int j = tid; j < nfc; j += kThreads) {
-    const Cand cd = gath[j];
-    const int c = cd.i / kChunk;
-    const float mc = st[c].m;
-    const float e = term_exact(temper_exact(cd.x, A.T, A.temper), Mp);
-    const double fast = (double)term_fast(cd.x, mc, A.a) * chunk_scale(A, mc, Mp);
-    const double corr = (double)e - fast;
-    atomicAdd(&sh.corr, (unsigned long long)__double2ll_rn(corr * 1125899906842624.0));  // 2^50
+  const int nf = F.nf;
+  const int ksum = (MODE == kTopK) ? A.k : min(A.ksum, nf);
+  if (nf > kGathMax || nf < ksum || ksum < 1) {
+    if (tid == 0) F.slow = 1;
   }
   __syncthreads();
-  if (tid == 0) sh.S = sh.S + (double)(long long)sh.corr * (1.0 / 1125899906842624.0);
+  const int nfc = min(nf, kGathMax);
+
+  // ---- the ksum-th largest logit; exact terms of everything >= it correct the
+  // sum.  Those candidates are first compacted into a dense list (aliasing
+  // keys) so the fp64 work runs on full warps.
+  Cand* top = reinterpret_cast<Cand*>(F.keys);
+  if (!F.slow) {
+    const float xk = kth_largest(F.gath, nfc, ksum, F.sel);
+    if (tid == 0) { F.xk = xk; F.nF = 0; }
+    __syncthreads();
+    for (int j0 = warp * 32; j0 < nfc; j0 += kThreads) {
+      const int j = j0 + lane;
+      const Cand cd = j < nfc ? F.gath[j] : Cand{-INFINITY, 0};
+      const bool keep = j < nfc && cd.x >= xk;
+      const unsigned msk = __ballot_sync(kAll, keep);
+      if (msk) {
+        int base = 0;
+        if (lane == 0) base = atomicAdd(&F.nF, __popc(msk));
+        base = __shfl_sync(kAll, base, 0);
+        const int pos = base + __popc(msk & ((1u << lane) - 1u));
+        if (keep && pos < kFinMax) top[pos] = cd;
+      }
+    }
+    __syncthreads();
+    const int ntop = F.nF;
+    if (ntop > kFinMax) {
+      if (tid == 0) F.slow = 1;
+    } else {
+      for (int j = tid; j < ntop; j += kThreads) {
+        const Cand cd = top[j];
+        const int c = cd.i / kChunk;
+        const float mc = c < kFinChunks ? F.cm[c] : __ldcg(&st[c].m);
+        const double sc = c < kFinChunks ? F.cs[c] : chunk_scale(A, mc, Mp);
+        const float e = term_exact(temper_exact(cd.x, A.T, A.temper), Mp);
+        const double fast = (double)term_fast(cd.x, mc, A.a) * sc;
+        atomicAdd(&F.corr, (unsigned long long)__double2ll_rn(((double)e - fast) * 1125899906842624.0));  // 2^50
+      }
+    }
+  }
   __syncthreads();
-  const double S = sh.S;
+  if (tid == 0) F.S = F.S_fast + (double)(long long)F.corr * (1.0 / 1125899906842624.0);
+  __syncthreads();
+  const double S = F.S;
 
   RowInfo R;
   R.row = A.logits + (int64_t)r * A.ld;
@@ -639,93 +643,88 @@ __global__ void __launch_bounds__(kThreads) finalize_kernel(const Args A) {
   R.Mp = Mp;
   R.S = S;
   R.a = A.a;
-  R.mscale = sh.scale0 / S;
+  R.mscale = F.scale0 / S;
   R.T = A.T;
   R.temper = A.temper;
 
-  if (MODE == kTopK && !sh.slow) {
-    // keys: (prob desc, id asc) as ascending 64-bit keys
-    for (int j = tid; j < nfc; j += kThreads) {
-      const Cand cd = gath[j];
-      const float p = prob_exact(term_exact(temper_exact(cd.x, A.T, A.temper), Mp), S);
-      sh.keys[j] = ((unsigned long long)(0xFFFFFFFFu - __float_as_uint(p)) << 32) | (uint32_t)cd.i;
+  if (MODE == kTopK && !F.slow) {
+    // Every element with prob == prob(x_k) must be in the list (x_lo >= tau_row).
+    // Usually the next fp32 value below x_k already has a smaller probability,
+    // so x_k is the low end of its tie group and no search is needed.
+    if (warp == 0) {
+      const float xk = F.xk;
+      bool search = false;
+      if (xk != -INFINITY) {
+        const float below = fkey_inv(fkey(xk) - 1u);
+        search = !(prob_of(R, below) < prob_of(R, xk));
+      }
+      const float lo = search ? tie_low(R, xk) : xk;
+      if (lane == 0) {
+        F.xlo = lo;
+        if (lo < tau_row) F.slow = 1;
+      }
     }
-    int np2 = 1;
-    while (np2 < nfc) np2 <<= 1;
-    for (int j = nfc + tid; j < np2; j += kThreads) sh.keys[j] = ~0ull;
     __syncthreads();
-    // bitonic sort ascending
-    for (int kk = 2; kk <= np2; kk <<= 1) {
-      for (int jj = kk >> 1; jj > 0; jj >>= 1) {
-        for (int i = tid; i < np2; i += kThreads) {
-          const int ixj = i ^ jj;
-          if (ixj > i) {
-            const unsigned long long x = sh.keys[i], y = sh.keys[ixj];
-            const bool asc = (i & kk) == 0;
-            if ((x > y) == asc) { sh.keys[i] = y; sh.keys[ixj] = x; }
-          }
-        }
+    if (!F.slow) {
+      const float xlo = F.xlo;
+      auto key_of = [&](const Cand cd) {
+        const float p = prob_exact(term_exact(temper_exact(cd.x, A.T, A.temper), Mp), S);
+        return ((unsigned long long)(0xFFFFFFFFu - __float_as_uint(p)) << 32) | (uint32_t)cd.i;
+      };
+      if (xlo == F.xk) {
+        // the dense list is the candidate set: keys in place
+        const int ntop = F.nF;
+        for (int j = tid; j < ntop; j += kThreads) F.keys[j] = key_of(top[j]);
+      } else {
         __syncthreads();
-      }
-    }
-    // completeness: every element outside the list has prob <= prob(pred(tau_row))
-    if (tid == 0) {
-      const int k = A.k;
-      if (nfc < k) {
-        sh.slow = 1;
-      } else if (tau_row != -INFINITY) {
-        const float pk = __uint_as_float(0xFFFFFFFFu - (uint32_t)(sh.keys[k - 1] >> 32));
-        const float below = fkey_inv(fkey(tau_row) - 1u);
-        const float pout = prob_of(R, below);
-        if (!(pk > pout)) sh.slow = 1;
-      }
-    }
-    __syncthreads();
-    if (!sh.slow) {
-      if (tid == 0) {
-        // src/generation.js:32-48, sequential fp64 as in the reference
-        int n = A.k;
-        if (A.use_topp) {
-          double acc = 0.0;
-          int cut = n;
-          for (int i = 0; i < n; i++) {
-            acc += (double)__uint_as_float(0xFFFFFFFFu - (uint32_t)(sh.keys[i] >> 32));
-            if (acc >= A.top_p) { cut = i + 1; break; }
+        if (tid == 0) F.nF = 0;
+        __syncthreads();
+        for (int j0 = warp * 32; j0 < nfc; j0 += kThreads) {
+          const int j = j0 + lane;
+          const Cand cd = j < nfc ? F.gath[j] : Cand{-INFINITY, 0};
+          const bool keep = j < nfc && cd.x >= xlo;
+          const unsigned msk = __ballot_sync(kAll, keep);
+          if (msk) {
+            int base = 0;
+            if (lane == 0) base = atomicAdd(&F.nF, __popc(msk));
+            base = __shfl_sync(kAll, base, 0);
+            const int pos = base + __popc(msk & ((1u << lane) - 1u));
+            if (keep && pos < kFinMax) F.keys[pos] = key_of(cd);
           }
-          n = cut > 1 ? cut : 1;
         }
-        double total = 0.0;
-        for (int i = 0; i < n; i++) total += (double)__uint_as_float(0xFFFFFFFFu - (uint32_t)(sh.keys[i] >> 32));
-        double rr = (A.u ? A.u[r] : 0.0) * total;
-        int id = (int)(uint32_t)sh.keys[n - 1];
-        for (int i = 0; i < n; i++) {
-          rr -= (double)__uint_as_float(0xFFFFFFFFu - (uint32_t)(sh.keys[i] >> 32));
-          if (rr <= 0.0) { id = (int)(uint32_t)sh.keys[i]; break; }
-        }
-        A.out_ids[r] = id;
-        if (A.d_n_cand) A.d_n_cand[r] = n;
-        if (A.d_total) A.d_total[r] = total;
-        if (A.d_row_max) A.d_row_max[r] = (double)Mp;
-        if (A.d_row_sum) A.d_row_sum[r] = S;
-        if (A.d_row_flags) A.d_row_flags[r] = 0;
-        sh.nf = n;
       }
       __syncthreads();
-      if (A.d_cand_ids || A.d_cand_probs) {
-        const int n = sh.nf;
-        for (int i = tid; i < n && i < A.cand_cap; i += kThreads) {
-          const unsigned long long kkey = sh.keys[i];
-          if (A.d_cand_ids) A.d_cand_ids[(int64_t)r * A.cand_cap + i] = (int32_t)(uint32_t)kkey;
-          if (A.d_cand_probs)
-            A.d_cand_probs[(int64_t)r * A.cand_cap + i] = __uint_as_float(0xFFFFFFFFu - (uint32_t)(kkey >> 32));
+      const int nF = F.nF;
+      if (nF > kFinMax || nF < A.k) {
+        if (tid == 0) F.slow = 1;
+      } else {
+        // rank sort (keys are distinct: the low word is the id), into gath's space
+        unsigned long long* sorted = reinterpret_cast<unsigned long long*>(F.gath);
+        for (int t = tid; t < nF; t += kThreads) {
+          const unsigned long long key = F.keys[t];
+          int rank = 0;
+          for (int j = 0; j < nF; j++) rank += F.keys[j] < key;
+          sorted[rank] = key;
         }
+        __syncthreads();
+        if (warp == 0) topk_draw(A, r, sorted, Mp, S, &F.nF);
+        __syncthreads();
+        if (A.d_cand_ids || A.d_cand_probs) {
+          const int n = F.nF;  // set by topk_draw
+          for (int i = tid; i < n && i < A.cand_cap; i += kThreads) {
+            const unsigned long long kkey = sorted[i];
+            if (A.d_cand_ids) A.d_cand_ids[(int64_t)r * A.cand_cap + i] = (int32_t)(uint32_t)kkey;
+            if (A.d_cand_probs)
+              A.d_cand_probs[(int64_t)r * A.cand_cap + i] = __uint_as_float(0xFFFFFFFFu - (uint32_t)(kkey >> 32));
+          }
+        }
+        return;
       }
-      return;
     }
+    __syncthreads();
   }
-
   // ---- exact rescan of the whole row
-  int flags = (MODE == kTopK) ? MS_ROW_SLOWPATH : 0;
+  const int flags = (MODE == kTopK) ? MS_ROW_SLOWPATH : 0;
   if (A.use_pen && A.penbits) {
     const int W = (V + 31) >> 5;
     uint32_t* pb = A.penbits + (int64_t)r * W;
@@ -736,6 +735,7 @@ __global__ void __launch_bounds__(kThreads) finalize_kernel(const Args A) {
       const int id = A.hist[h];
       if (id >= 0 && id < V) atomicOr(&pb[id >> 5], 1u << (id & 31));
     }
+    __threadfence_block();
     __syncthreads();
     R.pb = pb;
   }
@@ -743,48 +743,297 @@ __global__ void __launch_bounds__(kThreads) finalize_kernel(const Args A) {
     if (A.d_row_max) A.d_row_max[r] = (double)Mp;
     if (A.d_row_sum) A.d_row_sum[r] = S;
   }
-  full_path(A, r, R, sh.sel, flags);
-  (void)lane; (void)warp;
+  full_path(A, r, R, F.sel, flags);
 }
 
-// explicit instantiations
-template __global__ void chunk_kernel<kGreedy, false>(const Args);
-template __global__ void chunk_kernel<kGreedy, true>(const Args);
-template __global__ void chunk_kernel<kTopK, false>(const Args);
-template __global__ void chunk_kernel<kTopK, true>(const Args);
-template __global__ void chunk_kernel<kFull, false>(const Args);
-template __global__ void chunk_kernel<kFull, true>(const Args);
-template __global__ void finalize_kernel<kGreedy>(const Args);
-template __global__ void finalize_kernel<kTopK>(const Args);
-template __global__ void finalize_kernel<kFull>(const Args);
+// =============================================================== the kernel
+template <int MODE, bool PEN>
+__global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_constant__ Args A) {
+  extern __shared__ __align__(128) unsigned char dyn_smem[];
+  float* tile = reinterpret_cast<float*>(dyn_smem);
+  __shared__ __align__(8) uint64_t bar[kSub];
+  __shared__ uint32_t penmask[kChunk / 32];
+  __shared__ int is_last;
+  __shared__ Cand cq[kWarps][kWarpCap];
+  __shared__ int w_cnt[kWarps];
+  __shared__ float w_max[kWarps];
+  __shared__ uint32_t w_mk[kWarps], w_tk[kWarps];
+  __shared__ double w_sum[kWarps];
+  __shared__ int w_bi[kWarps];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int c = blockIdx.x, r = blockIdx.y;
+  const int c0 = c * kChunk;
+  const int n = min(kChunk, A.V - c0);
+  const float* g = A.logits + (int64_t)r * A.ld + c0;
+  const bool bulk = ((reinterpret_cast<uintptr_t>(g) & 15) == 0) && ((n & 3) == 0);
+
+  if (tid == 0) {
+    if (bulk) {
+      for (int s = 0; s < kSub; s++) mbar_init(&bar[s], 1);
+      fence_mbar_init();
+    }
+  }
+  if (PEN) penmask[tid] = 0u;  // kChunk / 32 == kThreads words
+  __syncthreads();
+  if (bulk) {
+    if (tid == 0) {
+      for (int s = 0; s < kSub; s++) {
+        const int b = s * kSubElems, cnt = min(kSubElems, n - b);
+        if (cnt > 0) {
+          mbar_expect_tx(&bar[s], (uint32_t)cnt * 4u);
+          bulk_g2s(tile + b, g + b, (uint32_t)cnt * 4u, &bar[s]);
+        }
+      }
+    }
+  } else {
+    for (int j = tid; j < n; j += kThreads) tile[j] = __ldg(g + j);
+  }
+  for (int j = n + tid; j < kChunk; j += kThreads) tile[j] = -INFINITY;
+
+  // ---- penalty bitmap of this chunk, built while the copies are in flight
+  if (PEN) {
+    const int64_t h0 = A.hist_off[r];
+    const int hn = (int)(A.hist_off[r + 1] - h0);
+    const int32_t* hrow = A.hist + h0;
+    for (int jb = 0; jb < hn; jb += 4 * kThreads) {
+      uint32_t ids[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const int j = jb + q * kThreads + tid;
+        ids[q] = j < hn ? (uint32_t)__ldg(hrow + j) : 0xFFFFFFFFu;
+      }
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const uint32_t d = ids[q] - (uint32_t)c0;  // ids outside [c0, c0+n) wrap past n
+        if (d < (uint32_t)n) atomicOr(&penmask[d >> 5], 1u << (d & 31));
+      }
+    }
+  }
+  // one thread waits for the copies; the rest park at the barrier
+  int timed_out = 0;
+  if (bulk && tid == 0) {
+    for (int s = 0; s < kSub; s++)
+      if (s * kSubElems < n && !mbar_wait(&bar[s], 0, kWaitCycles)) timed_out = 1;
+  }
+  if (__syncthreads_or(timed_out)) {
+    // The call fails (status word); the CTA still runs to the end on whatever
+    // the tile holds, so the row counters stay consistent.
+    if (tid == 0) {
+      atomicOr(A.status, kStatusTimeout);
+      if (bulk)  // let any copy still in flight land before going on (bounded)
+        for (int s = 0; s < kSub; s++)
+          if (s * kSubElems < n) mbar_wait(&bar[s], 0, kWaitCycles);
+    }
+    __syncthreads();
+  }
+
+  // ---- apply the penalty to the flagged logits (one bitmap word per thread)
+  if (PEN) {
+    uint32_t w = penmask[tid];
+    while (w) {
+      const int b = __ffs(w) - 1;
+      w &= w - 1;
+      const int j = tid * 32 + b;
+      tile[j] = pen_apply_fast(tile[j], A.pen, A.rpen);
+    }
+    __syncthreads();
+  }
+
+  const float4* t4 = reinterpret_cast<const float4*>(tile);
+  constexpr int kIters = kChunk / 4 / kThreads;  // 8 float4 per thread
+
+  if (MODE == kGreedy) {
+    // first index of the strict max (src/generation.js:51-55)
+    float bv = -INFINITY;
+    int bi = INT_MAX;
+#pragma unroll 4
+    for (int i = 0; i < kIters; i++) {
+      const int q = tid + i * kThreads;
+      const float4 v = t4[q];
+      const int j = c0 + 4 * q;
+      if (v.x > bv) { bv = v.x; bi = j; }
+      if (v.y > bv) { bv = v.y; bi = j + 1; }
+      if (v.z > bv) { bv = v.z; bi = j + 2; }
+      if (v.w > bv) { bv = v.w; bi = j + 3; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(kAll, bv, o);
+      const int oi = __shfl_xor_sync(kAll, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) { w_max[warp] = bv; w_bi[warp] = bi; }
+    __syncthreads();
+    if (tid == 0) {
+      for (int w = 1; w < kWarps; w++)
+        if (w_max[w] > bv || (w_max[w] == bv && w_bi[w] < bi)) { bv = w_max[w]; bi = w_bi[w]; }
+      ChunkStat st;
+      st.m = bv; st.tau = bv; st.s = 0.0; st.n_cand = 0; st.best_i = bi; st.best_v = bv; st.pad = 0;
+      A.stats[(int64_t)r * A.n_chunks + c] = st;
+    }
+  } else {
+    // ---- pass A: thread maxima -> chunk max and tau
+    float tm = -INFINITY;
+#pragma unroll 4
+    for (int i = 0; i < kIters; i++) {
+      const float4 v = t4[tid + i * kThreads];
+      tm = fmaxf(tm, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+    }
+    // The warp's kw-th largest thread maximum, by kw rounds of a warp max
+    // reduction over order-preserving keys, removing one instance per round.
+    // At least kw thread maxima of every warp are >= it, so tau = min over
+    // warps is reached by >= kWarps*kw >= top_k distinct elements of the chunk.
+    const uint32_t tkey = fkey(tm);  // tm is never NaN
+    const uint32_t wmk = __reduce_max_sync(kAll, tkey);
+    uint32_t kk = tkey, wtk = wmk;
+    for (int t = 0; t < A.kw; t++) {
+      wtk = __reduce_max_sync(kAll, kk);
+      const unsigned eq = __ballot_sync(kAll, kk == wtk);
+      if (lane == __ffs(eq) - 1) kk = 0u;  // below every float key
+    }
+    if (lane == 0) { w_mk[warp] = wmk; w_tk[warp] = wtk; }
+    __syncthreads();
+    const float m = fkey_inv(__reduce_max_sync(kAll, lane < kWarps ? w_mk[lane] : 0u));
+    const float tau = fkey_inv(__reduce_min_sync(kAll, lane < kWarps ? w_tk[lane] : 0xFFFFFFFFu));
+
+
+    // ---- pass B: fast exp sum (Kahan in fp32) and candidates >= tau.  Each
+    // warp appends to its own shared-memory queue (ballot + popc, no atomics);
+    // the queues are copied to the chunk's global slots at the end.
+    const float mref = (m == -INFINITY) ? 0.f : m;
+    const float a = A.a;
+    float s = 0.f, comp = 0.f;
+    int wc = 0;  // this warp's queue length (warp-uniform)
+    Cand* q = cq[warp];
+    const unsigned lt = (1u << lane) - 1u;
+    auto push = [&](bool p, float x, int idx) {
+      const unsigned b = __ballot_sync(kAll, p);
+      if (p) {
+        const int pos = wc + __popc(b & lt);
+        if (pos < kWarpCap) q[pos] = Cand{x, idx};
+      }
+      wc += __popc(b);
+    };
+    uint32_t cmask = 0;  // bit i: this thread's float4 of step i holds an element >= tau
+    auto step = [&](const float4 v, int j, int i, bool partial) {
+      float e0 = term_fast(v.x, mref, a), e1 = term_fast(v.y, mref, a);
+      float e2 = term_fast(v.z, mref, a), e3 = term_fast(v.w, mref, a);
+      if (partial) {  // padding past the row end contributes nothing
+        if (j >= n) e0 = 0.f;
+        if (j + 1 >= n) e1 = 0.f;
+        if (j + 2 >= n) e2 = 0.f;
+        if (j + 3 >= n) e3 = 0.f;
+      }
+      const float t = __fadd_rn(__fadd_rn(e0, e1), __fadd_rn(e2, e3));
+      const float y = __fsub_rn(t, comp);
+      const float ss = __fadd_rn(s, y);
+      comp = __fsub_rn(__fsub_rn(ss, s), y);
+      s = ss;
+      const float v4 = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+      cmask |= (uint32_t)(v4 >= tau) << i;
+    };
+    if (n == kChunk) {
+#pragma unroll 4
+      for (int i = 0; i < kIters; i++) {
+        const int qq = tid + i * kThreads;
+        step(t4[qq], 4 * qq, i, false);
+      }
+    } else {
+      for (int i = 0; i < kIters; i++) {
+        const int qq = tid + i * kThreads;
+        step(t4[qq], 4 * qq, i, true);
+      }
+    }
+    // candidates: only the flagged float4 are read again (about 1-2 rounds per warp)
+    while (__any_sync(kAll, cmask != 0)) {
+      const bool has = cmask != 0;
+      const int i = has ? __ffs(cmask) - 1 : 0;
+      cmask &= cmask - 1u;
+      const int qq = tid + i * kThreads;
+      const float4 v = t4[qq];
+      const int j = 4 * qq, gj = c0 + j;
+      push(has && v.x >= tau && j < n, v.x, gj);
+      push(has && v.y >= tau && j + 1 < n, v.y, gj + 1);
+      push(has && v.z >= tau && j + 2 < n, v.z, gj + 2);
+      push(has && v.w >= tau && j + 3 < n, v.w, gj + 3);
+    }
+    double ds = (double)s - (double)comp;
+    ds = warp_sum(ds);
+    if (lane == 0) { w_sum[warp] = ds; w_cnt[warp] = wc; }
+    __syncthreads();
+    // queue offsets; a full queue makes the chunk count exceed kCap (overflow)
+    int off = 0, tot = 0, ovf = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++) {
+      const int cw = w_cnt[w];
+      if (w < warp) off += cw;
+      tot += cw;
+      ovf |= cw > kWarpCap;
+    }
+    Cand* dst = A.cands + ((int64_t)r * A.n_chunks + c) * kCap;
+    const int mine = min(wc, kWarpCap);
+    for (int jj = lane; jj < mine; jj += 32)
+      if (off + jj < kCap) dst[off + jj] = q[jj];
+    if (tid == 0) {
+      double S = 0.0;
+      for (int w = 0; w < kWarps; w++) S += w_sum[w];
+      ChunkStat st;
+      st.m = m; st.tau = tau; st.s = S; st.n_cand = ovf ? kCap + 1 : tot;
+      st.best_i = INT_MAX; st.best_v = m; st.pad = 0;
+      A.stats[(int64_t)r * A.n_chunks + c] = st;
+    }
+  }
+
+  // ---- the last chunk of the row to finish finalizes it
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int old = atomicAdd(&A.row_count[r], 1);
+    is_last = (old == A.n_chunks - 1);
+    if (is_last) A.row_count[r] = 0;  // ready for the next call
+  }
+  __syncthreads();
+  if (is_last) {
+    __threadfence();
+    if (!(*((volatile int32_t*)A.status) & kStatusTimeout))
+      finalize_row<MODE>(A, r, *reinterpret_cast<FinSmem*>(dyn_smem));
+  }
+}
+
+static_assert(sizeof(FinSmem) <= kChunk * sizeof(float), "finalize scratch must fit in the chunk tile");
+static_assert(kChunk / 32 == kThreads, "one penalty bitmap word per thread");
 
 // =============================================================== launch
-size_t finalize_smem_bytes() { return sizeof(FinShared); }
+namespace {
+constexpr size_t kSmem = (size_t)kChunk * sizeof(float);
+
+template <int MODE, bool PEN>
+cudaError_t set_attrs() {
+  return cudaFuncSetAttribute((const void*)sample_kernel<MODE, PEN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)kSmem);
+}
+
+template <int MODE, bool PEN>
+cudaError_t launch_mode(const Args& S, dim3 grid, cudaStream_t stream) {
+  sample_kernel<MODE, PEN><<<grid, dim3(kThreads), kSmem, stream>>>(S);
+  return cudaGetLastError();
+}
+}  // namespace
 
 cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev) {
-  const dim3 block(kThreads);
-  const size_t chunk_smem = (size_t)kChunk * sizeof(float);
-  const size_t fin_smem = sizeof(FinShared);
   static bool attrs_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attrs_done[dev]) {
-#define MS_SET_ATTR(fn, bytes)                                                                   \
-  do {                                                                                           \
-    cudaError_t e_ = cudaFuncSetAttribute((const void*)fn, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                          (int)(bytes));                                         \
-    if (e_ != cudaSuccess) return e_;                                                            \
-  } while (0)
-    MS_SET_ATTR((chunk_kernel<kGreedy, false>), chunk_smem);
-    MS_SET_ATTR((chunk_kernel<kGreedy, true>), chunk_smem);
-    MS_SET_ATTR((chunk_kernel<kTopK, false>), chunk_smem);
-    MS_SET_ATTR((chunk_kernel<kTopK, true>), chunk_smem);
-    MS_SET_ATTR((chunk_kernel<kFull, false>), chunk_smem);
-    MS_SET_ATTR((chunk_kernel<kFull, true>), chunk_smem);
-    MS_SET_ATTR(finalize_kernel<kGreedy>, fin_smem);
-    MS_SET_ATTR(finalize_kernel<kTopK>, fin_smem);
-    MS_SET_ATTR(finalize_kernel<kFull>, fin_smem);
-#undef MS_SET_ATTR
+    cudaError_t e = cudaSuccess;
+    if (e == cudaSuccess) e = set_attrs<kGreedy, false>();
+    if (e == cudaSuccess) e = set_attrs<kGreedy, true>();
+    if (e == cudaSuccess) e = set_attrs<kTopK, false>();
+    if (e == cudaSuccess) e = set_attrs<kTopK, true>();
+    if (e == cudaSuccess) e = set_attrs<kFull, false>();
+    if (e == cudaSuccess) e = set_attrs<kFull, true>();
+    if (e != cudaSuccess) return e;
     attrs_done[dev] = true;
   }
   // rows in slices of at most 65535 (grid.y limit)
@@ -796,6 +1045,7 @@ cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev) {
     if (A.hist_off) S.hist_off = A.hist_off + r0;
     if (A.u) S.u = A.u + r0;
     S.stats = A.stats + r0 * A.n_chunks;
+    S.row_count = A.row_count + r0;
     S.cands = A.cands + r0 * A.n_chunks * kCap;
     if (A.penbits) S.penbits = A.penbits + r0 * ((A.V + 31) / 32);
     S.out_ids = A.out_ids + r0;
@@ -806,32 +1056,23 @@ cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev) {
     if (A.d_row_sum) S.d_row_sum = A.d_row_sum + r0;
     if (A.d_total) S.d_total = A.d_total + r0;
     if (A.d_row_flags) S.d_row_flags = A.d_row_flags + r0;
-    const dim3 grid_c(A.n_chunks, rows);
+    const dim3 grid(A.n_chunks, rows);
     const bool pen = A.use_pen != 0;
-    const bool prof = ev != nullptr && r0 == 0 && A.B <= 65535;
+    const bool prof = ev != nullptr && r0 == 0;
     if (prof) cudaEventRecord(ev[0], stream);
+    cudaError_t e;
     switch (A.mode) {
       case kGreedy:
-        if (pen) chunk_kernel<kGreedy, true><<<grid_c, block, chunk_smem, stream>>>(S);
-        else chunk_kernel<kGreedy, false><<<grid_c, block, chunk_smem, stream>>>(S);
-        if (prof) cudaEventRecord(ev[1], stream);
-        finalize_kernel<kGreedy><<<rows, block, 0, stream>>>(S);
+        e = pen ? launch_mode<kGreedy, true>(S, grid, stream) : launch_mode<kGreedy, false>(S, grid, stream);
         break;
       case kTopK:
-        if (pen) chunk_kernel<kTopK, true><<<grid_c, block, chunk_smem, stream>>>(S);
-        else chunk_kernel<kTopK, false><<<grid_c, block, chunk_smem, stream>>>(S);
-        if (prof) cudaEventRecord(ev[1], stream);
-        finalize_kernel<kTopK><<<rows, block, fin_smem, stream>>>(S);
+        e = pen ? launch_mode<kTopK, true>(S, grid, stream) : launch_mode<kTopK, false>(S, grid, stream);
         break;
       default:
-        if (pen) chunk_kernel<kFull, true><<<grid_c, block, chunk_smem, stream>>>(S);
-        else chunk_kernel<kFull, false><<<grid_c, block, chunk_smem, stream>>>(S);
-        if (prof) cudaEventRecord(ev[1], stream);
-        finalize_kernel<kFull><<<rows, block, fin_smem, stream>>>(S);
+        e = pen ? launch_mode<kFull, true>(S, grid, stream) : launch_mode<kFull, false>(S, grid, stream);
         break;
     }
-    if (prof) cudaEventRecord(ev[2], stream);
-    const cudaError_t e = cudaGetLastError();
+    if (prof) { cudaEventRecord(ev[1], stream); cudaEventRecord(ev[2], stream); }
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
