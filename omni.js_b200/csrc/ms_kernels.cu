@@ -31,293 +31,21 @@
 #include <cstdio>
 
 #include "ms_device.cuh"
+#include "ms_fullpath.cuh"
 
 namespace ms {
 
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s: bound on every wait
 constexpr unsigned kAll = 0xffffffffu;
 constexpr int kWarps = kThreads / 32;
-constexpr int kWarpCap = 32;  // candidate queue slots per warp and chunk
+constexpr int kWarpCap = 64;  // candidate queue slots per warp and chunk
 constexpr int kFinChunks = 256;  // chunks whose scale the finalizer caches
 
-// =============================================================== full-row path
-struct RowInfo {
-  const float* row;
-  int V;
-  const uint32_t* pb;  // penalty bitmap of the row (null: no penalty)
-  double pen;
-  float M;             // max of the penalised row
-  float Mp;            // fp32(M / T): the reference's mx
-  double S;            // softmax denominator
-  float a;
-  double mscale;       // fast mass of x = term_fast(x, M, a) * mscale  (~ prob)
-  double T;
-  int temper;
-};
-
-struct SelShared {
+// =============================================================== shared scratch
+struct SelShared {  // kth_largest's radix state
   int cnt[256];
-  double mass[256];
-  double above;
-  uint32_t prefix;
   int digit, rem;
-  double total_w;
-  int red_i[kWarps];
-  int red_i2[kWarps];
-  double red_d[kWarps];
-  unsigned long long pre[kThreads];
-  int result;
-  float lohi[2];
-  float pstar;
 };
-
-__device__ __forceinline__ float load_x(const RowInfo& R, int i) {
-  float v = __ldg(R.row + i);
-  if (R.pb && ((R.pb[i >> 5] >> (i & 31)) & 1u)) v = pen_apply(v, R.pen);
-  return v;
-}
-__device__ __forceinline__ double mass_fast(const RowInfo& R, float x) {
-  return (double)term_fast(x, R.M, R.a) * R.mscale;
-}
-__device__ __forceinline__ float prob_of(const RowInfo& R, float x) {
-  return prob_exact(term_exact(temper_exact(x, R.T, R.temper), R.Mp), R.S);
-}
-
-// Value v of the row such that W(x > v) < target <= W(x >= v), where W counts
-// elements (by_mass false) or sums their fast probability mass.  Only
-// non-empty buckets qualify; a target above the total selects the smallest
-// element.
-__device__ float radix_select(const RowInfo& R, bool by_mass, double target, SelShared& sh) {
-  const int tid = threadIdx.x;
-  uint32_t prefix = 0, pmask = 0;
-  double above = 0.0;
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int d = tid; d < 256; d += kThreads) { sh.cnt[d] = 0; sh.mass[d] = 0.0; }
-    __syncthreads();
-    for (int i = tid; i < R.V; i += kThreads) {
-      const float x = load_x(R, i);
-      if (x != x) continue;
-      const uint32_t k = fkey(x);
-      if ((k & pmask) == prefix) {
-        const int d = (k >> shift) & 255;
-        atomicAdd(&sh.cnt[d], 1);
-        if (by_mass) atomicAdd(&sh.mass[d], mass_fast(R, x));
-      }
-    }
-    __syncthreads();
-    if (tid == 0) {
-      double cum = above;
-      int chosen = -1, last = -1;
-      for (int d = 255; d >= 0; d--) {
-        if (sh.cnt[d] == 0) continue;
-        last = d;
-        const double w = by_mass ? sh.mass[d] : (double)sh.cnt[d];
-        if (cum + w >= target) { chosen = d; break; }
-        cum += w;
-      }
-      if (chosen < 0) {
-        chosen = last < 0 ? 0 : last;
-        if (last >= 0) cum -= by_mass ? sh.mass[chosen] : (double)sh.cnt[chosen];
-      }
-      sh.above = cum;
-      sh.prefix = prefix | ((uint32_t)chosen << shift);
-    }
-    __syncthreads();
-    above = sh.above;
-    prefix = sh.prefix;
-    pmask |= 0xFFu << shift;
-    __syncthreads();
-  }
-  return fkey_inv(prefix);
-}
-
-// Keys [lo, hi] with pred(lo) true and pred monotone (true, then false as the
-// key grows): returns the largest key with pred true.  One warp evaluates 32
-// probes per round.  `dir` -1 searches downward (pred true at hi, returns the
-// smallest key with pred true).
-template <typename Pred>
-__device__ uint32_t warp_boundary_search(uint32_t lo, uint32_t hi, int dir, Pred pred) {
-  const int lane = threadIdx.x & 31;
-  const uint64_t base = dir > 0 ? lo : hi;
-  uint64_t L = 0, H = (uint64_t)hi - lo;
-  while (H > L) {
-    const uint64_t step = (H - L + 31) / 32;
-    uint64_t p = L + (uint64_t)(lane + 1) * step;
-    if (p > H) p = H;
-    const uint32_t key = dir > 0 ? (uint32_t)(base + p) : (uint32_t)(base - p);
-    const bool t = pred(key);
-    const unsigned msk = __ballot_sync(kAll, t);
-    const int ntrue = __popc(msk);
-    const uint64_t p_last = __shfl_sync(kAll, p, ntrue > 0 ? ntrue - 1 : 0);
-    const uint64_t p_next = __shfl_sync(kAll, p, ntrue < 32 ? ntrue : 31);
-    if (ntrue == 0) {
-      H = p_next - 1;
-    } else {
-      L = p_last;
-      if (ntrue < 32) H = p_next - 1;
-      else if (p_last >= H) H = L;
-    }
-  }
-  return dir > 0 ? (uint32_t)(base + L) : (uint32_t)(base - L);
-}
-
-// Smallest / largest x (fp32) with prob_of(x) == prob_of(v), searched by one
-// full warp of the caller; v itself qualifies.
-__device__ float tie_low(const RowInfo& R, float v) {
-  const float pv = prob_of(R, v);
-  const uint32_t kv = fkey(v);
-  const uint32_t kNegInf = fkey(-INFINITY);
-  auto same = [&](uint32_t key) { return prob_of(R, fkey_inv(key)) == pv; };
-  return fkey_inv(warp_boundary_search(kNegInf <= kv ? kNegInf : kv, kv, -1, same));
-}
-__device__ float tie_high(const RowInfo& R, float v) {
-  const float pv = prob_of(R, v);
-  const uint32_t kv = fkey(v);
-  const uint32_t kM = fkey(R.M) > kv ? fkey(R.M) : kv;
-  auto same = [&](uint32_t key) { return prob_of(R, fkey_inv(key)) == pv; };
-  return fkey_inv(warp_boundary_search(kv, kM, +1, same));
-}
-
-struct GroupSel {
-  int index;       // vocabulary id of the selected element
-  int64_t rank;    // 1-based position in (prob desc, id asc) order
-  double cum;      // fast cumulative mass through it
-};
-
-// Resolve the tie group of v (all x with prob_of(x) == prob_of(v)), then the
-// element reaching `target` (count or fast mass) inside it in id order.
-__device__ GroupSel resolve_group(const RowInfo& R, float v, bool by_mass, double target,
-                                  SelShared& sh) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (warp == 0) {
-    const float lo = tie_low(R, v), hi = tie_high(R, v);
-    if (lane == 0) { sh.lohi[0] = lo; sh.lohi[1] = hi; sh.pstar = prob_of(R, v); }
-  }
-  __syncthreads();
-  const float xlo = sh.lohi[0], xhi = sh.lohi[1], pstar = sh.pstar;
-  int c_hi = 0, c_g = 0;
-  double m_hi = 0.0;
-  for (int i = tid; i < R.V; i += kThreads) {
-    const float x = load_x(R, i);
-    if (x > xhi) { c_hi++; m_hi += mass_fast(R, x); }
-    else if (x >= xlo) c_g++;
-  }
-  c_hi = warp_sum_i(c_hi);
-  c_g = warp_sum_i(c_g);
-  m_hi = warp_sum(m_hi);
-  if (lane == 0) { sh.red_i[warp] = c_hi; sh.red_i2[warp] = c_g; sh.red_d[warp] = m_hi; }
-  __syncthreads();
-  int64_t CH = 0, CG = 0;
-  double MH = 0.0;
-  for (int w = 0; w < kWarps; w++) { CH += sh.red_i[w]; CG += sh.red_i2[w]; MH += sh.red_d[w]; }
-  __syncthreads();
-  int64_t j;
-  if (by_mass) {
-    const double need = target - MH;
-    if (need <= 0.0) j = 1;
-    else if (pstar > 0.f) j = (int64_t)ceil(need / (double)pstar);
-    else j = CG;
-  } else {
-    j = (int64_t)target - CH;
-  }
-  if (j < 1) j = 1;
-  if (j > CG) j = CG;
-  // j-th group element in id order: contiguous segment per thread, scan.
-  const int seg = (R.V + kThreads - 1) / kThreads;
-  const int s0 = min(R.V, tid * seg), s1 = min(R.V, s0 + seg);
-  int cnt = 0;
-  for (int i = s0; i < s1; i++) {
-    const float x = load_x(R, i);
-    cnt += (x >= xlo && x <= xhi);
-  }
-  sh.pre[tid] = (unsigned long long)cnt;
-  if (tid == 0) sh.result = -1;
-  __syncthreads();
-  if (tid == 0) {
-    unsigned long long run = 0;
-    for (int t = 0; t < kThreads; t++) { const unsigned long long c = sh.pre[t]; sh.pre[t] = run; run += c; }
-  }
-  __syncthreads();
-  const int64_t before = (int64_t)sh.pre[tid];
-  if (before < j && before + cnt >= j) {
-    int64_t need = j - before;
-    for (int i = s0; i < s1; i++) {
-      const float x = load_x(R, i);
-      if (x >= xlo && x <= xhi && --need == 0) { sh.result = i; break; }
-    }
-  }
-  __syncthreads();
-  GroupSel gsel;
-  gsel.index = sh.result < 0 ? 0 : sh.result;
-  gsel.rank = CH + j;
-  gsel.cum = MH + (double)j * (double)pstar;
-  __syncthreads();
-  return gsel;
-}
-
-__device__ GroupSel select_rank(const RowInfo& R, int64_t k, SelShared& sh) {
-  const float v = radix_select(R, false, (double)k, sh);
-  return resolve_group(R, v, false, (double)k, sh);
-}
-__device__ GroupSel select_mass(const RowInfo& R, double target, SelShared& sh) {
-  const float v = radix_select(R, true, target, sh);
-  return resolve_group(R, v, true, target, sh);
-}
-
-// Exact top-k / top-p / draw over the whole row (src/generation.js:27-49).
-__device__ __noinline__ void full_path(const Args& A, int r, const RowInfo& R, SelShared& sh, int flags) {
-  const int tid = threadIdx.x;
-  const int V = R.V;
-  const bool use_k = A.k > 0 && A.k < V;
-  int64_t n;
-  double mass_n;
-  int last_id;  // id at rank n (fallback of the draw loop)
-  if (use_k) {
-    const GroupSel gk = select_rank(R, A.k, sh);
-    n = A.k;
-    mass_n = gk.cum;
-    last_id = gk.index;
-  } else {
-    double t = 0.0;
-    for (int i = tid; i < V; i += kThreads) {
-      const float x = load_x(R, i);
-      if (x == x) t += mass_fast(R, x);
-    }
-    t = warp_sum(t);
-    if ((tid & 31) == 0) sh.red_d[tid >> 5] = t;
-    __syncthreads();
-    mass_n = 0.0;
-    for (int w = 0; w < kWarps; w++) mass_n += sh.red_d[w];
-    __syncthreads();
-    n = V;
-    last_id = -1;
-  }
-  double total = mass_n;
-  if (A.use_topp && mass_n >= A.top_p) {
-    const GroupSel gp = select_mass(R, A.top_p, sh);
-    if (gp.rank < n) {
-      n = gp.rank < 1 ? 1 : gp.rank;
-      total = gp.cum;
-      last_id = gp.index;
-    }
-  }
-  if (last_id < 0) last_id = select_rank(R, n, sh).index;
-  const double u = A.u ? A.u[r] : 0.0;
-  const double rr = u * total;
-  int id;
-  if (rr <= 0.0) {
-    id = select_rank(R, 1, sh).index;
-  } else {
-    const GroupSel gd = select_mass(R, rr, sh);
-    id = (gd.rank > n) ? last_id : gd.index;
-  }
-  if (tid == 0) {
-    A.out_ids[r] = id;
-    if (A.d_n_cand) A.d_n_cand[r] = (int32_t)n;
-    if (A.d_total) A.d_total[r] = total;
-    if (A.d_row_flags) A.d_row_flags[r] = flags | MS_ROW_FULLVOCAB;
-  }
-}
 
 // =============================================================== finalize
 struct FinSmem {
@@ -646,6 +374,8 @@ __device__ __noinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   R.mscale = F.scale0 / S;
   R.T = A.T;
   R.temper = A.temper;
+  R.rpen = A.rpen;
+  R.nat16 = (float)(16.0 / A.T);
 
   if (MODE == kTopK && !F.slow) {
     // Every element with prob == prob(x_k) must be in the list (x_lo >= tau_row).
@@ -743,7 +473,8 @@ __device__ __noinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
     if (A.d_row_max) A.d_row_max[r] = (double)Mp;
     if (A.d_row_sum) A.d_row_sum[r] = S;
   }
-  full_path(A, r, R, F.sel, flags);
+  __syncthreads();  // the finalize scratch is reused by the full-row path
+  full_path(A, r, R, *reinterpret_cast<FullSmem*>(&F), flags);
 }
 
 // =============================================================== the kernel
@@ -1002,6 +733,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
 }
 
 static_assert(sizeof(FinSmem) <= kChunk * sizeof(float), "finalize scratch must fit in the chunk tile");
+static_assert(sizeof(FullSmem) <= kChunk * sizeof(float), "full-row scratch must fit in the chunk tile");
 static_assert(kChunk / 32 == kThreads, "one penalty bitmap word per thread");
 
 // =============================================================== launch
