@@ -158,6 +158,38 @@ int ms_profile_read(ms_ctx* ctx, double* stream_ms, double* finalize_ms, int64_t
  */
 int ms_scratch_bytes(int64_t B, int64_t V, const ms_params* params, int64_t* out_bytes);
 
+/*
+ * ms_sample without a context and without allocating.  No counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc.  Examples are a
+ * host program whose own allocator already reserved the device memory, or a
+ * latency-critical decode loop where a cudaMalloc (which may synchronize the
+ * device) is not acceptable.
+ *
+ * Device pointers only, on the caller's `stream` (NULL = default stream).  The
+ * arguments mean what they mean for ms_sample; there are no diagnostics.
+ *
+ * Scratch.  The call does not allocate.  It uses a fixed device array of
+ * MS_NOALLOC_SCRATCH_BYTES inside this library, which every GPU that loads the
+ * library holds until the process exits.  A call whose scratch would exceed it
+ * returns MS_ERR_SCRATCH; ms_scratch_bytes plus about 4*B + 512 bytes is what a
+ * call needs.  Each call clears the parts that must start at zero.  Calls whose
+ * work overlaps on the GPU (on different streams, or different host threads)
+ * share the array and race: order them on one stream.
+ *
+ * Set-up.  The first call on each device looks up the array's device address
+ * there (cudaGetSymbolAddress), with that device current.  Make that first call
+ * before any stream capture.
+ *
+ * Returns MS_OK, MS_ERR_ARG, MS_ERR_SCRATCH, MS_ERR_STATE or MS_ERR_CUDA.  No
+ * message is kept (there is no context).  A kernel wait that runs out is not
+ * reported by this call.
+ */
+#define MS_NOALLOC_SCRATCH_BYTES (8u << 20)
+#define MS_ERR_SCRATCH  -7   /* ms_sample_noalloc: the call needs more than MS_NOALLOC_SCRATCH_BYTES */
+int ms_sample_noalloc(const float* logits, int64_t B, int64_t V, int64_t ld,
+                      const int32_t* hist, const int64_t* hist_off, const ms_params* params,
+                      const double* u, int32_t* out_ids, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <algorithm>
 #include <array>
@@ -462,4 +463,84 @@ extern "C" int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V,
   }
   cudaSetDevice(prev);
   return rc;
+}
+
+// ====================================================== allocation-free entry point
+// Scratch for ms_sample_noalloc: a file-scope device array, so the call never
+// allocates.  Every GPU that loads this library holds these bytes until the
+// process exits.  Host code must not use the symbol's name as an address (it
+// is a host-side stand-in); the device address comes from
+// cudaGetSymbolAddress, taken once per device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MS_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};  // device address of g_noalloc_scratch, per device
+}  // namespace
+
+extern "C" int ms_sample_noalloc(const float* logits, int64_t B, int64_t V, int64_t ld, const int32_t* hist,
+                                 const int64_t* hist_off, const ms_params* params, const double* u,
+                                 int32_t* out_ids, void* stream) {
+  if (!params || B < 0 || V < 1 || V > (int64_t)INT32_MAX / 2 || ld < V) return MS_ERR_ARG;
+  if (B == 0) return MS_OK;
+  if (!logits || !out_ids) return MS_ERR_ARG;
+  if (hist_off != nullptr && hist == nullptr) return MS_ERR_ARG;
+  if (hist_off == nullptr) hist = nullptr;
+  const ms_params pp = *params;
+  const Plan P = make_plan(V, &pp, hist != nullptr);
+  if (P.mode != ms::kGreedy && !u) return MS_ERR_ARG;
+  // [row counters | status word | the kernel's scratch], all inside the array
+  const size_t cnt_bytes = align_up((size_t)B * 4, 256);
+  const ScratchLayout L = scratch_layout(B, V, P);
+  const size_t need = cnt_bytes + 256 + L.total;
+  if (need > (size_t)MS_NOALLOC_SCRATCH_BYTES) return MS_ERR_SCRATCH;
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return MS_ERR_STATE;
+  void* addr = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return MS_ERR_CUDA;
+      g_noalloc_addr[dev] = p;
+    }
+    addr = g_noalloc_addr[dev];
+  }
+  char* base = (char*)addr;
+  cudaStream_t st = (cudaStream_t)stream;
+  // the array keeps the last call's contents: counters and status restart at zero
+  if (cudaMemsetAsync(base, 0, cnt_bytes + 256, st) != cudaSuccess) return MS_ERR_CUDA;
+  char* scratch = base + cnt_bytes + 256;
+
+  ms::Args A;
+  memset(&A, 0, sizeof A);
+  A.logits = logits;
+  A.ld = ld;
+  A.B = (int32_t)B;
+  A.V = (int32_t)V;
+  A.hist = hist;
+  A.hist_off = hist_off;
+  A.pen = pp.repetition_penalty;
+  A.rpen = 1.0 / pp.repetition_penalty;
+  A.use_pen = P.use_pen;
+  A.mode = P.mode;
+  A.T = pp.temperature;
+  A.temper = P.temper;
+  A.a = P.a;
+  A.k = P.k;
+  A.kw = P.kw;
+  A.use_topp = P.use_topp;
+  A.top_p = pp.top_p;
+  A.u = u;
+  A.n_chunks = P.n_chunks;
+  A.stats = (ms::ChunkStat*)(scratch + L.stats);
+  A.cands = (ms::Cand*)(scratch + L.cands);
+  A.penbits = (P.use_pen && P.mode != ms::kGreedy) ? (uint32_t*)(scratch + L.penbits) : nullptr;
+  A.status = (int32_t*)(base + cnt_bytes);
+  A.row_count = (int32_t*)base;
+  A.ksum = ms::kKSum;
+  A.out_ids = out_ids;
+  if (ms::launch_sample(A, st, nullptr) != cudaSuccess) return MS_ERR_CUDA;
+  return MS_OK;
 }

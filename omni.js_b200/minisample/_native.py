@@ -18,6 +18,9 @@ MS_ERR_NCCL = -3
 MS_ERR_TIMEOUT = -4
 MS_ERR_OOM = -5
 MS_ERR_STATE = -6
+MS_ERR_SCRATCH = -7
+
+MS_NOALLOC_SCRATCH_BYTES = 8 << 20
 
 MS_HOST_PTRS = 0x1
 MS_DEVICE_PTRS = 0x2
@@ -33,11 +36,12 @@ MS_ROW_SLOWPATH = 0x8
 ERROR_NAMES = {
     MS_ERR_ARG: "MS_ERR_ARG", MS_ERR_CUDA: "MS_ERR_CUDA", MS_ERR_NCCL: "MS_ERR_NCCL",
     MS_ERR_TIMEOUT: "MS_ERR_TIMEOUT", MS_ERR_OOM: "MS_ERR_OOM", MS_ERR_STATE: "MS_ERR_STATE",
+    MS_ERR_SCRATCH: "MS_ERR_SCRATCH",
 }
 
 # Every symbol include/minisample.h declares.
 EXPORTED = ("ms_version", "ms_create", "ms_destroy", "ms_last_error", "ms_sample", "ms_profile_read",
-            "ms_scratch_bytes")
+            "ms_scratch_bytes", "ms_sample_noalloc")
 
 
 class MsParams(ctypes.Structure):
@@ -103,6 +107,11 @@ def load(path: str | None = None):
     L.ms_scratch_bytes.restype = ctypes.c_int
     L.ms_scratch_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.POINTER(MsParams),
                                    ctypes.POINTER(ctypes.c_int64)]
+    L.ms_sample_noalloc.restype = ctypes.c_int
+    L.ms_sample_noalloc.argtypes = [
+        ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,
+        ctypes.POINTER(MsParams), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+    ]
     if path is None:
         _lib = L
     return L
