@@ -38,7 +38,7 @@ L2_BYTES = 126 * 1024 * 1024
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="minisample", choices=["minisample", "reference"])
     ap.add_argument("--workload", default="gemma_b512")
@@ -70,7 +70,7 @@ def committed_traffic(workload):
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -91,11 +91,13 @@ class ClockSampler:
         try:
             self.out = open(os.devnull, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"] + sel, stdout=subprocess.PIPE, stderr=self.out, text=True)
+                                          "-lms", "50"] + sel, stdout=subprocess.PIPE, stderr=self.out, text=True)
         except Exception:
             self.proc = None
 
-    def stop(self):
+    def stop(self, t0=None, t1=None):
+        """Median SM clock and throttle reasons of the samples taken between
+        wall times t0 and t1 (all samples if none fall inside)."""
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -104,23 +106,29 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
             text = ""
-        sm, mx, reasons = [], [], set()
+        import datetime
+
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        samples = []
         for line in text.splitlines():
             f = [c.strip() for c in line.split(",")]
-            if len(f) < 9:
+            if len(f) < 10:
                 continue
             try:
-                sm.append(float(f[1]))
-                mx.append(float(f[2]))
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                sm, mx = float(f[2]), float(f[3])
             except ValueError:
                 continue
-            for nm, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(nm)
-        if not sm:
+            rs = {nm for nm, v in zip(names, f[6:10]) if v.lower().startswith("active")}
+            samples.append((ts, sm, mx, rs))
+        if not samples:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+        inside = [x for x in samples if t0 is not None and t0 <= x[0] <= t1] or samples
+        reasons = set()
+        for x in inside:
+            reasons |= x[3]
+        return {"sm_mhz": statistics.median(x[1] for x in inside), "sm_max_mhz": max(x[2] for x in inside),
+                "samples": len(inside), "in_window": len(inside) < len(samples) or t0 is None,
                 "reasons": sorted(reasons)}
 
 
@@ -222,7 +230,8 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     torch.cuda.synchronize()
     clocks.start()
-    time.sleep(0.3)  # let the sampler see the first samples
+    time.sleep(0.5)  # the sampler's first samples
+    w0 = time.time()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
@@ -230,7 +239,8 @@ def run_ours(args, rank, world, local_rank):
         step(i, profile=True)
     e1.record(stream)
     stream.synchronize()
-    clk = clocks.stop()
+    w1 = time.time()
+    clk = clocks.stop(w0, w1)
     barrier()
     ms = e0.elapsed_time(e1) / args.steps
     chunk_ms, fin_ms, calls = sampler.profile_read()
