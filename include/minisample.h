@@ -145,12 +145,23 @@ int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V, int64_t ld
  * Kernel time of the calls made with MS_PROFILE since the last read, summed
  * over calls (milliseconds, CUDA events on the launch stream):
  *   stream_ms    the chunk kernel, which reads every logit once
- *   finalize_ms  the per-row finalize kernel
+ *   finalize_ms  the per-row finalize kernel; 0 when the chunk kernel's last
+ *                CTA of each row finalizes it (greedy rows, or
+ *                MS_SPLIT_FINALIZE=0 in the environment), whose time is then
+ *                part of stream_ms
+ * In a profiled call an event sits between the two kernels, so the finalize
+ * cannot start early; profile a sample of the calls, not all of them.
  * Waits for those calls' events.  No reference counterpart: the reference
  * has no profiling hooks (its demo times with performance.now(),
  * demo.template.html:230,295).
  */
 int ms_profile_read(ms_ctx* ctx, double* stream_ms, double* finalize_ms, int64_t* calls);
+
+/*
+ * Kernels this context has launched (all its devices, since ms_create): one
+ * or two per ms_sample call and per 65535 rows.  No reference counterpart.
+ */
+int ms_launch_count(ms_ctx* ctx, int64_t* kernels);
 
 /*
  * Bytes of device scratch that ms_sample needs for a [B, V] call with these

@@ -3,6 +3,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -13,7 +14,7 @@
 #include "ms_device.cuh"
 
 namespace ms {
-cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev);
+cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev, int64_t* launched);
 size_t finalize_smem_bytes();
 }  // namespace ms
 
@@ -31,6 +32,7 @@ struct DevState {
   int64_t counters_cap = 0;
   std::vector<std::array<cudaEvent_t, 3>> prof_pending;  // MS_PROFILE calls not yet read
   std::vector<std::array<cudaEvent_t, 3>> prof_free;
+  int64_t launches = 0;  // kernels launched on this device
 };
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -71,6 +73,19 @@ Plan make_plan(int64_t V, const ms_params* p, bool have_hist) {
   if (P.kw < 1) P.kw = 1;
   if (P.kw > 32) P.kw = 32;
   return P;
+}
+
+// Sampled rows are finalized by a second grid (1, the default) or by the
+// stream kernel's last CTA per row (0); MS_SPLIT_FINALIZE in the environment
+// overrides the default.  Greedy rows always take the last-CTA form, whose
+// finalize is a few comparisons.
+int split_finalize_default() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("MS_SPLIT_FINALIZE");
+    v = (e && *e) ? (atoi(e) != 0) : 1;
+  }
+  return v;
 }
 
 struct ScratchLayout {
@@ -220,6 +235,14 @@ int ms_profile_read(ms_ctx* c, double* stream_ms, double* finalize_ms, int64_t* 
   return MS_OK;
 }
 
+int ms_launch_count(ms_ctx* c, int64_t* kernels) {
+  if (!c || !kernels) return MS_ERR_ARG;
+  int64_t n = 0;
+  for (auto& s : c->devs) n += s.launches;
+  *kernels = n;
+  return MS_OK;
+}
+
 int ms_scratch_bytes(int64_t B, int64_t V, const ms_params* params, int64_t* out_bytes) {
   if (!params || !out_bytes || B < 0 || V < 1) return MS_ERR_ARG;
   const Plan P = make_plan(V, params, true);
@@ -278,6 +301,7 @@ static int run_device(ms_ctx* ctx, DevState& s, const float* logits, int64_t B, 
   A.status = s.status;
   A.row_count = s.counters;
   A.ksum = ms::kKSum;
+  A.split_finalize = (P.mode != ms::kGreedy) ? split_finalize_default() : 0;
   A.out_ids = out_ids;
   if (diag) {
     A.cand_cap = diag->cand_cap;
@@ -301,7 +325,7 @@ static int run_device(ms_ctx* ctx, DevState& s, const float* logits, int64_t B, 
     s.prof_free.pop_back();
     ev = s.prof_pending.back().data();
   }
-  MS_CUDA(ctx, ms::launch_sample(A, stream, ev));
+  MS_CUDA(ctx, ms::launch_sample(A, stream, ev, &s.launches));
   return MS_OK;
 }
 
@@ -541,6 +565,6 @@ extern "C" int ms_sample_noalloc(const float* logits, int64_t B, int64_t V, int6
   A.row_count = (int32_t*)base;
   A.ksum = ms::kKSum;
   A.out_ids = out_ids;
-  if (ms::launch_sample(A, st, nullptr) != cudaSuccess) return MS_ERR_CUDA;
+  if (ms::launch_sample(A, st, nullptr, nullptr) != cudaSuccess) return MS_ERR_CUDA;
   return MS_OK;
 }

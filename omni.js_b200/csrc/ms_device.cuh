@@ -34,12 +34,12 @@ constexpr int kStatusTimeout = 0x1;
 
 struct ChunkStat {
   float m;        // max of the penalised logits of the chunk (NaN ignored; -inf if none)
-  float tau;      // candidate threshold: at least top_k elements of the chunk are >= tau
+  float tau;      // top-k bound: at least top_k elements of the chunk are >= tau (-inf if unknown)
   double s;       // sum of fast exp2((x - m) * a) over the chunk (NaN if a NaN appeared)
   int32_t n_cand; // elements >= tau (only the first kCap are stored)
   int32_t best_i; // greedy: first index of the max (INT32_MAX if nothing > -inf)
   float best_v;   // greedy: that max
-  int32_t pad;
+  float sig;      // storage threshold: every element >= sig is among the candidates (sig >= tau)
 };
 
 struct Cand {
@@ -75,6 +75,7 @@ struct Args {
   uint32_t* penbits;     // [B, ceil(V/32)] penalty bitmap (slow path), may be null
   int32_t* out_ids;      // [B]
   int32_t* status;       // device status word
+  int32_t split_finalize; // 1: rows are finalized by a separate finalize_kernel grid
   // diagnostics (each may be null)
   int32_t cand_cap;
   int32_t* d_cand_ids;

@@ -13,9 +13,11 @@
 //   3. pass A: chunk max and a threshold tau that at least top_k elements of
 //      the chunk reach (from the sorted per-thread maxima of every warp);
 //   4. pass B: fast fp32 sum of 2^((x - m) * log2(e)/T) and the list of
-//      elements >= tau;
-//   5. the chunk results go to global scratch; the last CTA of the row to
-//      finish (atomic row counter) finalizes the row: softmax denominator
+//      elements >= tau (>= sig, a storage threshold, in a partial chunk);
+//   5. the chunk results go to global scratch; the row is finalized either by
+//      the last CTA of the row to finish (atomic row counter) or by a second
+//      grid of one CTA per row, launched as a programmatic dependent of the
+//      first (greedy rows always use the first form): softmax denominator
 //      (fast sum corrected with the exact terms of the top candidates), the
 //      exact fp32 probabilities of the candidates, their order
 //      (prob desc, id asc), top-k, top-p and the draw (src/generation.js:9-17,
@@ -234,13 +236,14 @@ __device__ __noinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
 
   // ---- row max, NaN detection, overflow, tau_row, fast sum
   if (warp == 0) {
-    float M = -INFINITY, tr = -INFINITY;
+    float M = -INFINITY, tr = -INFINITY, sg = -INFINITY;
     int nanr = 0, ovf = 0;
     for (int c = lane; c < A.n_chunks; c += 32) {
       const float m = __ldcg(&st[c].m), t = __ldcg(&st[c].tau);
       const double s = __ldcg(&st[c].s);
       M = fmaxf(M, m);
       tr = fmaxf(tr, t);
+      sg = fmaxf(sg, __ldcg(&st[c].sig));
       nanr |= (s != s);
       ovf |= (__ldcg(&st[c].n_cand) > kCap);
     }
@@ -248,6 +251,7 @@ __device__ __noinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
     for (int o = 16; o > 0; o >>= 1) {
       M = fmaxf(M, __shfl_xor_sync(kAll, M, o));
       tr = fmaxf(tr, __shfl_xor_sync(kAll, tr, o));
+      sg = fmaxf(sg, __shfl_xor_sync(kAll, sg, o));
       nanr |= __shfl_xor_sync(kAll, nanr, o);
       ovf |= __shfl_xor_sync(kAll, ovf, o);
     }
@@ -265,7 +269,8 @@ __device__ __noinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
     }
     if (lane == 0) {
       F.M = M; F.Mp = Mp; F.tau_row = tr; F.nan_row = nanr; F.overflow = ovf;
-      F.nf = 0; F.slow = ovf; F.corr = 0ull; F.S_fast = S;
+      // a chunk that kept only elements >= sig > tau_row may miss candidates
+      F.nf = 0; F.slow = ovf | (sg > tr); F.corr = 0ull; F.S_fast = S;
       F.scale0 = nanr ? 0.0 : exp((double)M / A.T - (double)Mp);
     }
   }
@@ -600,7 +605,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
       for (int w = 1; w < kWarps; w++)
         if (w_max[w] > bv || (w_max[w] == bv && w_bi[w] < bi)) { bv = w_max[w]; bi = w_bi[w]; }
       ChunkStat st;
-      st.m = bv; st.tau = bv; st.s = 0.0; st.n_cand = 0; st.best_i = bi; st.best_v = bv; st.pad = 0;
+      st.m = bv; st.tau = bv; st.s = 0.0; st.n_cand = 0; st.best_i = bi; st.best_v = bv; st.sig = bv;
       A.stats[(int64_t)r * A.n_chunks + c] = st;
     }
   } else {
@@ -615,10 +620,15 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     // reduction over order-preserving keys, removing one instance per round.
     // At least kw thread maxima of every warp are >= it, so tau = min over
     // warps is reached by >= kWarps*kw >= top_k distinct elements of the chunk.
+    // A partial chunk (n < 4 * kThreads) has data in its first w_act warps
+    // only, and takes a larger per-warp rank so those warps still cover keff.
+    const int keff = (MODE == kTopK) ? A.k : A.ksum;
+    const int w_act = min(kWarps, ((n + 3) / 4 + 31) / 32);
+    const int kwc = (n >= 4 * kThreads) ? A.kw : min(32, (keff + w_act - 1) / w_act);
     const uint32_t tkey = fkey(tm);  // tm is never NaN
     const uint32_t wmk = __reduce_max_sync(kAll, tkey);
     uint32_t kk = tkey, wtk = wmk;
-    for (int t = 0; t < A.kw; t++) {
+    for (int t = 0; t < kwc; t++) {
       wtk = __reduce_max_sync(kAll, kk);
       const unsigned eq = __ballot_sync(kAll, kk == wtk);
       if (lane == __ffs(eq) - 1) kk = 0u;  // below every float key
@@ -626,7 +636,19 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     if (lane == 0) { w_mk[warp] = wmk; w_tk[warp] = wtk; }
     __syncthreads();
     const float m = fkey_inv(__reduce_max_sync(kAll, lane < kWarps ? w_mk[lane] : 0u));
-    const float tau = fkey_inv(__reduce_min_sync(kAll, lane < kWarps ? w_tk[lane] : 0xFFFFFFFFu));
+    // Warps whose kwc-th thread maximum is -inf (padding past the row end, or
+    // -inf logits) are left out of the minimum.  The minimum over the others
+    // is the chunk's top-k bound tau when they alone hold keff elements
+    // (kwc each); otherwise tau = -inf.  sig is the storage threshold: every
+    // element >= sig becomes a candidate, and the finalizer falls back to the
+    // exact rescan when some chunk's sig is above the row's tau.
+    const uint32_t wk = lane < kWarps ? w_tk[lane] : 0u;
+    const bool wok = wk > fkey(-INFINITY);
+    const int n_ok = __popc(__ballot_sync(kAll, wok));
+    const float tmin = n_ok ? fkey_inv(__reduce_min_sync(kAll, wok ? wk : 0xFFFFFFFFu)) : -INFINITY;
+    const float tau = (n_ok * kwc >= keff) ? tmin : -INFINITY;
+    // a chunk too small for a bound keeps everything when it fits one queue
+    const float sig = (tau == -INFINITY && n <= kWarpCap) ? -INFINITY : tmin;
 
 
     // ---- pass B: fast exp sum (Kahan in fp32) and candidates >= tau.  Each
@@ -662,7 +684,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
       comp = __fsub_rn(__fsub_rn(ss, s), y);
       s = ss;
       const float v4 = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
-      cmask |= (uint32_t)(v4 >= tau) << i;
+      cmask |= (uint32_t)(v4 >= sig) << i;
     };
     if (n == kChunk) {
 #pragma unroll 4
@@ -684,10 +706,10 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
       const int qq = tid + i * kThreads;
       const float4 v = t4[qq];
       const int j = 4 * qq, gj = c0 + j;
-      push(has && v.x >= tau && j < n, v.x, gj);
-      push(has && v.y >= tau && j + 1 < n, v.y, gj + 1);
-      push(has && v.z >= tau && j + 2 < n, v.z, gj + 2);
-      push(has && v.w >= tau && j + 3 < n, v.w, gj + 3);
+      push(has && v.x >= sig && j < n, v.x, gj);
+      push(has && v.y >= sig && j + 1 < n, v.y, gj + 1);
+      push(has && v.z >= sig && j + 2 < n, v.z, gj + 2);
+      push(has && v.w >= sig && j + 3 < n, v.w, gj + 3);
     }
     double ds = (double)s - (double)comp;
     ds = warp_sum(ds);
@@ -711,12 +733,18 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
       for (int w = 0; w < kWarps; w++) S += w_sum[w];
       ChunkStat st;
       st.m = m; st.tau = tau; st.s = S; st.n_cand = ovf ? kCap + 1 : tot;
-      st.best_i = INT_MAX; st.best_v = m; st.pad = 0;
+      st.best_i = INT_MAX; st.best_v = m; st.sig = sig;
       A.stats[(int64_t)r * A.n_chunks + c] = st;
     }
   }
 
-  // ---- the last chunk of the row to finish finalizes it
+  // ---- the last chunk of the row to finish finalizes it (unless a separate
+  // finalize kernel follows)
+  if (A.split_finalize) {
+    // let the finalize grid launch while the last chunks stream
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    return;
+  }
   __threadfence();
   __syncthreads();
   if (tid == 0) {
@@ -730,6 +758,16 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     if (!(*((volatile int32_t*)A.status) & kStatusTimeout))
       finalize_row<MODE>(A, r, *reinterpret_cast<FinSmem*>(dyn_smem));
   }
+}
+
+// Row finalize as its own grid (one CTA per row), launched as a programmatic
+// dependent of sample_kernel: it waits for the whole stream grid's writes.
+template <int MODE>
+__global__ void __launch_bounds__(kThreads) finalize_kernel(const __grid_constant__ Args A) {
+  extern __shared__ __align__(128) unsigned char fin_smem[];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (*((volatile int32_t*)A.status) & kStatusTimeout) return;
+  finalize_row<MODE>(A, blockIdx.x, *reinterpret_cast<FinSmem*>(fin_smem));
 }
 
 static_assert(sizeof(FinSmem) <= kChunk * sizeof(float), "finalize scratch must fit in the chunk tile");
@@ -746,14 +784,35 @@ cudaError_t set_attrs() {
                               (int)kSmem);
 }
 
+constexpr size_t kFinSmem = sizeof(FullSmem) > sizeof(FinSmem) ? sizeof(FullSmem) : sizeof(FinSmem);
+
+template <int MODE>
+cudaError_t set_fin_attrs() {
+  return cudaFuncSetAttribute((const void*)finalize_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)kFinSmem);
+}
+
 template <int MODE, bool PEN>
-cudaError_t launch_mode(const Args& S, dim3 grid, cudaStream_t stream) {
+cudaError_t launch_mode(const Args& S, dim3 grid, cudaStream_t stream, cudaEvent_t mid) {
   sample_kernel<MODE, PEN><<<grid, dim3(kThreads), kSmem, stream>>>(S);
-  return cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
+  if (mid) cudaEventRecord(mid, stream);
+  if (e != cudaSuccess || !S.split_finalize) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(S.B);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kFinSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, finalize_kernel<MODE>, S);
 }
 }  // namespace
 
-cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev) {
+cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev, int64_t* launched) {
   static bool attrs_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -765,6 +824,9 @@ cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev) {
     if (e == cudaSuccess) e = set_attrs<kTopK, true>();
     if (e == cudaSuccess) e = set_attrs<kFull, false>();
     if (e == cudaSuccess) e = set_attrs<kFull, true>();
+    if (e == cudaSuccess) e = set_fin_attrs<kGreedy>();
+    if (e == cudaSuccess) e = set_fin_attrs<kTopK>();
+    if (e == cudaSuccess) e = set_fin_attrs<kFull>();
     if (e != cudaSuccess) return e;
     attrs_done[dev] = true;
   }
@@ -792,20 +854,22 @@ cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev) {
     const bool pen = A.use_pen != 0;
     const bool prof = ev != nullptr && r0 == 0;
     if (prof) cudaEventRecord(ev[0], stream);
+    cudaEvent_t mid = prof ? ev[1] : nullptr;
     cudaError_t e;
     switch (A.mode) {
       case kGreedy:
-        e = pen ? launch_mode<kGreedy, true>(S, grid, stream) : launch_mode<kGreedy, false>(S, grid, stream);
+        e = pen ? launch_mode<kGreedy, true>(S, grid, stream, mid) : launch_mode<kGreedy, false>(S, grid, stream, mid);
         break;
       case kTopK:
-        e = pen ? launch_mode<kTopK, true>(S, grid, stream) : launch_mode<kTopK, false>(S, grid, stream);
+        e = pen ? launch_mode<kTopK, true>(S, grid, stream, mid) : launch_mode<kTopK, false>(S, grid, stream, mid);
         break;
       default:
-        e = pen ? launch_mode<kFull, true>(S, grid, stream) : launch_mode<kFull, false>(S, grid, stream);
+        e = pen ? launch_mode<kFull, true>(S, grid, stream, mid) : launch_mode<kFull, false>(S, grid, stream, mid);
         break;
     }
-    if (prof) { cudaEventRecord(ev[1], stream); cudaEventRecord(ev[2], stream); }
+    if (prof) cudaEventRecord(ev[2], stream);
     if (e != cudaSuccess) return e;
+    if (launched) *launched += S.split_finalize ? 2 : 1;
   }
   return cudaSuccess;
 }

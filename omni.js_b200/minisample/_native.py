@@ -41,7 +41,7 @@ ERROR_NAMES = {
 
 # Every symbol include/minisample.h declares.
 EXPORTED = ("ms_version", "ms_create", "ms_destroy", "ms_last_error", "ms_sample", "ms_profile_read",
-            "ms_scratch_bytes", "ms_sample_noalloc")
+            "ms_scratch_bytes", "ms_sample_noalloc", "ms_launch_count")
 
 
 class MsParams(ctypes.Structure):
@@ -104,6 +104,8 @@ def load(path: str | None = None):
     L.ms_profile_read.restype = ctypes.c_int
     L.ms_profile_read.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
                                   ctypes.POINTER(ctypes.c_int64)]
+    L.ms_launch_count.restype = ctypes.c_int
+    L.ms_launch_count.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64)]
     L.ms_scratch_bytes.restype = ctypes.c_int
     L.ms_scratch_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.POINTER(MsParams),
                                    ctypes.POINTER(ctypes.c_int64)]

@@ -90,6 +90,12 @@ class Sampler:
         self._check(self._L.ms_profile_read(self._ctx, ctypes.byref(a), ctypes.byref(b), ctypes.byref(n)))
         return a.value, b.value, n.value
 
+    def launch_count(self) -> int:
+        """Kernels this context has launched since it was created."""
+        n = ctypes.c_int64()
+        self._check(self._L.ms_launch_count(self._ctx, ctypes.byref(n)))
+        return n.value
+
     # ------------------------------------------------------------------ host
     def _sample_host(self, logits, params, u, hist, hist_off, diag, cand_cap, row_sharded, out, profile=False):
         if _is_torch(logits):

@@ -204,6 +204,37 @@ def test_workload_parity(oracle, sampler, name, B):
     print(f"{name}: {B} rows, {len(tol)} boundary rows")
 
 
+@pytest.mark.parametrize("name,B", [("gpt2_b1", 16), ("llama3_b64", 16), ("gemma_b512", 16)])
+def test_topk_rows_stay_on_candidate_path(oracle, sampler, name, B):
+    """Rows with top_k <= 256 on these distributions are finalized from the
+    chunk candidates, without the exact rescan (row flag 0x8), including a
+    vocabulary whose last chunk is short (50257 = 3 * 16384 + 1105)."""
+    w, X, hist, off, u = _workload(name, B)
+    ids_r, d_r, ids_g, d_g = run_both(oracle, sampler, X, w.params, u, hist, off)
+    check(ids_r, d_r, ids_g, d_g, w.params, name)
+    slow = int(np.sum((d_g["row_flags"] & 0x8) != 0))
+    assert slow == 0, f"{name}: {slow}/{B} rows took the rescan"
+
+
+@pytest.mark.parametrize("tail", [1, 63, 64, 65, 700, 1105, 2047, 2048, 2049])
+@pytest.mark.parametrize("k", [50, 256])
+def test_short_last_chunk(oracle, sampler, tail, k):
+    """Rows of 2 full chunks plus a short one, against the oracle."""
+    from minisample import SampleParams
+
+    rng = np.random.default_rng(tail * 7 + k)
+    V = 2 * 16384 + tail
+    X = rng.normal(0.0, 2.0, (6, V)).astype(np.float32)
+    X[1, -tail:] += 6.0          # the short chunk holds the largest logits
+    X[2, : 2 * 16384] = -np.inf  # only the short chunk is finite
+    sp = SampleParams(True, 0.8, k, 0.9, 1.0)
+    u = rng.random(6)
+    ids_r, d_r, ids_g, d_g = run_both(oracle, sampler, X, sp, u)
+    check(ids_r, d_r, ids_g, d_g, sp, f"tail {tail} k {k}", max_boundary_frac=0.34)
+    if k == 50 and tail >= 700:  # a short last chunk still bounds its candidates
+        assert not d_g["row_flags"][0] & 0x8, d_g["row_flags"]
+
+
 def test_gpt2_b1_generation_loop(oracle, sampler):
     """256 single-row steps, history = 64 prior ids + ids sampled so far; the
     penalty starts once something was generated (src/generation.js:73)."""
