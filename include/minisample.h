@@ -120,7 +120,8 @@ const char* ms_last_error(ms_ctx* ctx);
 /*
  * Sample one token id per row.  Replaces `pickToken(lastLogits, generated,
  * inputIds, opts)` (src/generation.js:71-81), applied to each of B rows.
- *   logits    [B, ld] fp32, ld >= V (row stride in elements)
+ *   logits    [B, ld] fp32, ld >= V (row stride in elements);
+ *             1 <= V <= 65535 * 16384 (1,073,725,440)
  *   hist      concatenated per-row id histories (int32), may be NULL when
  *             every row is empty; ids outside [0, V) are ignored, repeated ids
  *             count once (the reference builds a Set, src/generation.js:20)
@@ -159,7 +160,9 @@ int ms_profile_read(ms_ctx* ctx, double* stream_ms, double* finalize_ms, int64_t
 
 /*
  * Kernels this context has launched (all its devices, since ms_create): one
- * or two per ms_sample call and per 65535 rows.  No reference counterpart.
+ * per ms_sample call when greedy, two when sampled (the chunk kernel and the
+ * row finalize), per slice of rows (a slice holds about 2^31 / ceil(V/16384)
+ * rows).  No reference counterpart.
  */
 int ms_launch_count(ms_ctx* ctx, int64_t* kernels);
 

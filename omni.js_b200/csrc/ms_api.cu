@@ -66,26 +66,13 @@ Plan make_plan(int64_t V, const ms_params* p, bool have_hist) {
   } else {
     P.mode = ms::kFull;
   }
-  // every warp's kw-th largest thread maximum; kWarps * kw >= keff
+  // every warp's kw-th largest thread maximum; warps * kw >= keff
   const int warps = ms::kThreads / 32;
   const int keff = (P.mode == ms::kTopK) ? P.k : ms::kKSum;
   P.kw = (keff + warps - 1) / warps;
   if (P.kw < 1) P.kw = 1;
   if (P.kw > 32) P.kw = 32;
   return P;
-}
-
-// Sampled rows are finalized by a second grid (1, the default) or by the
-// stream kernel's last CTA per row (0); MS_SPLIT_FINALIZE in the environment
-// overrides the default.  Greedy rows always take the last-CTA form, whose
-// finalize is a few comparisons.
-int split_finalize_default() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("MS_SPLIT_FINALIZE");
-    v = (e && *e) ? (atoi(e) != 0) : 1;
-  }
-  return v;
 }
 
 struct ScratchLayout {
@@ -301,7 +288,6 @@ static int run_device(ms_ctx* ctx, DevState& s, const float* logits, int64_t B, 
   A.status = s.status;
   A.row_count = s.counters;
   A.ksum = ms::kKSum;
-  A.split_finalize = (P.mode != ms::kGreedy) ? split_finalize_default() : 0;
   A.out_ids = out_ids;
   if (diag) {
     A.cand_cap = diag->cand_cap;
@@ -335,7 +321,7 @@ extern "C" int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V,
   if (!ctx) return MS_ERR_ARG;
   if (!params) return fail(ctx, MS_ERR_ARG, "ms_sample: params is NULL");
   if (B < 0) return fail(ctx, MS_ERR_ARG, "ms_sample: B < 0");
-  if (V < 1 || V > (int64_t)INT32_MAX / 2) return fail(ctx, MS_ERR_ARG, "ms_sample: V out of range");
+  if (V < 1 || V > (int64_t)65535 * ms::kChunk) return fail(ctx, MS_ERR_ARG, "ms_sample: V out of range");
   if (ld < V) return fail(ctx, MS_ERR_ARG, "ms_sample: ld < V");
   if (B == 0) return MS_OK;
   if (!logits || !out_ids) return fail(ctx, MS_ERR_ARG, "ms_sample: logits/out_ids is NULL");
@@ -505,7 +491,7 @@ void* g_noalloc_addr[64] = {};  // device address of g_noalloc_scratch, per devi
 extern "C" int ms_sample_noalloc(const float* logits, int64_t B, int64_t V, int64_t ld, const int32_t* hist,
                                  const int64_t* hist_off, const ms_params* params, const double* u,
                                  int32_t* out_ids, void* stream) {
-  if (!params || B < 0 || V < 1 || V > (int64_t)INT32_MAX / 2 || ld < V) return MS_ERR_ARG;
+  if (!params || B < 0 || V < 1 || V > (int64_t)65535 * ms::kChunk || ld < V) return MS_ERR_ARG;
   if (B == 0) return MS_OK;
   if (!logits || !out_ids) return MS_ERR_ARG;
   if (hist_off != nullptr && hist == nullptr) return MS_ERR_ARG;

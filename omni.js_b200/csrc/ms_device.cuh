@@ -38,7 +38,7 @@ struct ChunkStat {
   double s;       // sum of fast exp2((x - m) * a) over the chunk (NaN if a NaN appeared)
   int32_t n_cand; // elements >= tau (only the first kCap are stored)
   int32_t best_i; // greedy: first index of the max (INT32_MAX if nothing > -inf)
-  float best_v;   // greedy: that max
+  float zref;     // fast terms are 2^(x * a - zref); NaN: 2^((x - m) * a) (m * a beyond fp32)
   float sig;      // storage threshold: every element >= sig is among the candidates (sig >= tau)
 };
 
@@ -75,7 +75,6 @@ struct Args {
   uint32_t* penbits;     // [B, ceil(V/32)] penalty bitmap (slow path), may be null
   int32_t* out_ids;      // [B]
   int32_t* status;       // device status word
-  int32_t split_finalize; // 1: rows are finalized by a separate finalize_kernel grid
   // diagnostics (each may be null)
   int32_t cand_cap;
   int32_t* d_cand_ids;
@@ -132,6 +131,44 @@ __device__ __forceinline__ float ex2_approx(float z) {
 __device__ __forceinline__ float term_fast(float x, float m, float a) {
   return ex2_approx(__fmul_rn(__fsub_rn(x, m), a));
 }
+// The chunk kernel's form of the fast term: 2^(x * a - zref), one fused
+// multiply-add, with zref = fp32(m * a) for the chunk max m.  Relative to
+// term_fast(x, m, a) the whole chunk carries the factor 2^(m * a - zref),
+// which the finalizer folds into the chunk's scale.
+__device__ __forceinline__ float term_fast_z(float x, float a, float zref) {
+  return ex2_approx(__fmaf_rn(x, a, -zref));
+}
+
+// ---------------------------------------------------------------- paired fp32 (sm_100)
+// Two fp32 lanes in one 64-bit register: fma / add on both at once, each lane
+// rounded exactly like the scalar instruction.
+__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(unsigned long long v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b,
+                                                     unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// max of three (NaN inputs are ignored, as by fmaxf)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 
 // ---------------------------------------------------------------- float keys
 // Order-preserving map of fp32 to uint32 (larger float -> larger key).
@@ -166,6 +203,20 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
           smem_addr(dst)),
       "l"(src), "r"(bytes), "r"(smem_addr(bar))
       : "memory");
+}
+// 4-byte asynchronous copy global -> shared (any 4-byte aligned address).
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+// The barrier's pending count goes up by one now, and comes down once the
+// thread's earlier cp.async copies have landed.
+__device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+// Orders this thread's earlier generic-proxy accesses of shared memory before
+// its later async-proxy (bulk copy) accesses.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 // Bounded wait on phase `parity`; false when ~`max_cycles` passed first.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long long max_cycles) {

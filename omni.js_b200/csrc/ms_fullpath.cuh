@@ -539,7 +539,7 @@ __device__ FullSel select_full(const RowInfo& R, FullSmem& sm, bool by_mass, dou
 }
 
 // Top-k / top-p / draw for one row over the whole vocabulary (src/generation.js:27-49).
-__device__ __noinline__ void full_path(const Args& A, int r, const RowInfo& R, FullSmem& sm, int flags) {
+__device__ __forceinline__ void full_path(const Args& A, int r, const RowInfo& R, FullSmem& sm, int flags) {
   const int tid = threadIdx.x;
   const int V = R.V;
   block_hist(R, sm.h0, [](float) { return true; }, [&](float x) { return bin0(R, x); });

@@ -31,6 +31,7 @@
 #include <cfloat>
 #include <climits>
 #include <cstdio>
+#include <algorithm>
 
 #include "ms_device.cuh"
 #include "ms_fullpath.cuh"
@@ -40,7 +41,6 @@ namespace ms {
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s: bound on every wait
 constexpr unsigned kAll = 0xffffffffu;
 constexpr int kWarps = kThreads / 32;
-constexpr int kWarpCap = 64;  // candidate queue slots per warp and chunk
 constexpr int kFinChunks = 256;  // chunks whose scale the finalizer caches
 
 // =============================================================== shared scratch
@@ -59,12 +59,23 @@ struct FinSmem {
   double S, S_fast, scale0;
   float M, Mp, tau_row, xk, xlo;
   float cm[kFinChunks];      // chunk maxima (first kFinChunks chunks)
+  float cz[kFinChunks];      // their fast-term offsets
   double cs[kFinChunks];     // chunk_scale of each
 };
 
-__device__ __forceinline__ double chunk_scale(const Args& A, float mc, float Mp) {
-  // exp(m_c / T - M'): converts a chunk's fast terms to the reference's units
-  return (mc == -INFINITY) ? 0.0 : exp((double)mc / A.T - (double)Mp);
+__device__ __forceinline__ double chunk_scale(const Args& A, float mc, float zc, float Mp) {
+  // exp(m_c / T - M') converts fast terms relative to the chunk max to the
+  // reference's units.  2^(x*a - zref) = 2^((x - m_c)*a) * 2^(m_c*a - zref), so
+  // 2^(zref - m_c*a) (the exponent is exact in fp64) undoes zref's rounding.
+  if (mc == -INFINITY) return 0.0;
+  double sc = exp((double)mc / A.T - (double)Mp);
+  if (zc == zc) sc *= exp2((double)zc - (double)mc * (double)A.a);
+  return sc;
+}
+
+// a chunk's fast term of x, recomputed bit for bit
+__device__ __forceinline__ float chunk_term(const Args& A, float x, float mc, float zc) {
+  return (zc == zc) ? term_fast_z(x, A.a, zc) : term_fast(x, mc, A.a);
 }
 
 // k-th largest x (1 <= k <= n) of the gathered candidates: radix select on
@@ -201,7 +212,7 @@ __device__ void topk_draw(const Args& A, int r, const unsigned long long* sorted
 }
 
 template <int MODE>
-__device__ __noinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
+__device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const ChunkStat* st = A.stats + (int64_t)r * A.n_chunks;
   const int V = A.V;
@@ -211,7 +222,7 @@ __device__ __noinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
       float bv = -INFINITY;
       int bi = INT_MAX;
       for (int c = lane; c < A.n_chunks; c += 32) {
-        const float v = __ldcg(&st[c].best_v);
+        const float v = __ldcg(&st[c].m);
         const int i = __ldcg(&st[c].best_i);
         if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
       }
@@ -260,10 +271,10 @@ __device__ __noinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
     double S = 0.0;
     if (!nanr) {
       for (int c = lane; c < A.n_chunks; c += 32) {
-        const float m = __ldcg(&st[c].m);
-        const double sc = chunk_scale(A, m, Mp);
+        const float m = __ldcg(&st[c].m), z = __ldcg(&st[c].zref);
+        const double sc = chunk_scale(A, m, z, Mp);
         if (m != -INFINITY) S += __ldcg(&st[c].s) * sc;
-        if (c < kFinChunks) { F.cm[c] = m; F.cs[c] = sc; }
+        if (c < kFinChunks) { F.cm[c] = m; F.cz[c] = z; F.cs[c] = sc; }
       }
       S = warp_sum(S);
     }
@@ -355,9 +366,10 @@ __device__ __noinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
         const Cand cd = top[j];
         const int c = cd.i / kChunk;
         const float mc = c < kFinChunks ? F.cm[c] : __ldcg(&st[c].m);
-        const double sc = c < kFinChunks ? F.cs[c] : chunk_scale(A, mc, Mp);
+        const float zc = c < kFinChunks ? F.cz[c] : __ldcg(&st[c].zref);
+        const double sc = c < kFinChunks ? F.cs[c] : chunk_scale(A, mc, zc, Mp);
         const float e = term_exact(temper_exact(cd.x, A.T, A.temper), Mp);
-        const double fast = (double)term_fast(cd.x, mc, A.a) * sc;
+        const double fast = (double)chunk_term(A, cd.x, mc, zc) * sc;
         atomicAdd(&F.corr, (unsigned long long)__double2ll_rn(((double)e - fast) * 1125899906842624.0));  // 2^50
       }
     }
@@ -490,15 +502,14 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
   __shared__ __align__(8) uint64_t bar[kSub];
   __shared__ uint32_t penmask[kChunk / 32];
   __shared__ int is_last;
-  __shared__ Cand cq[kWarps][kWarpCap];
-  __shared__ int w_cnt[kWarps];
+  __shared__ int q_cnt;  // candidates found (may exceed kCap: overflow)
   __shared__ float w_max[kWarps];
   __shared__ uint32_t w_mk[kWarps], w_tk[kWarps];
   __shared__ double w_sum[kWarps];
   __shared__ int w_bi[kWarps];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int c = blockIdx.x, r = blockIdx.y;
+  const int r = blockIdx.x, c = blockIdx.y;  // chunk-major: a row's earlier chunks run first
   const int c0 = c * kChunk;
   const int n = min(kChunk, A.V - c0);
   const float* g = A.logits + (int64_t)r * A.ld + c0;
@@ -511,6 +522,11 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     }
   }
   if (PEN) penmask[tid] = 0u;  // kChunk / 32 == kThreads words
+  if (tid == 0) q_cnt = 0;
+  // bound published by the row's chunks that ran earlier (0: none yet); the
+  // per-row counters serve sampled rows as this word, reset by the finalizer
+  uint32_t* row_pub = reinterpret_cast<uint32_t*>(A.row_count);
+  const uint32_t pub = (MODE != kGreedy) ? __ldcg(&row_pub[r]) : 0u;
   __syncthreads();
   if (bulk) {
     if (tid == 0) {
@@ -605,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
       for (int w = 1; w < kWarps; w++)
         if (w_max[w] > bv || (w_max[w] == bv && w_bi[w] < bi)) { bv = w_max[w]; bi = w_bi[w]; }
       ChunkStat st;
-      st.m = bv; st.tau = bv; st.s = 0.0; st.n_cand = 0; st.best_i = bi; st.best_v = bv; st.sig = bv;
+      st.m = bv; st.tau = bv; st.s = 0.0; st.n_cand = 0; st.best_i = bi; st.zref = 0.f; st.sig = bv;
       A.stats[(int64_t)r * A.n_chunks + c] = st;
     }
   } else {
@@ -614,7 +630,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
 #pragma unroll 4
     for (int i = 0; i < kIters; i++) {
       const float4 v = t4[tid + i * kThreads];
-      tm = fmaxf(tm, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
+      tm = fmax3(fmax3(tm, v.x, v.y), v.z, v.w);
     }
     // The warp's kw-th largest thread maximum, by kw rounds of a warp max
     // reduction over order-preserving keys, removing one instance per round.
@@ -647,101 +663,99 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     const int n_ok = __popc(__ballot_sync(kAll, wok));
     const float tmin = n_ok ? fkey_inv(__reduce_min_sync(kAll, wok ? wk : 0xFFFFFFFFu)) : -INFINITY;
     const float tau = (n_ok * kwc >= keff) ? tmin : -INFINITY;
-    // a chunk too small for a bound keeps everything when it fits one queue
-    const float sig = (tau == -INFINITY && n <= kWarpCap) ? -INFINITY : tmin;
+    // A chunk too small for a bound keeps everything when it fits its list.
+    // The row bound that the row's earlier chunks published (pub, at most
+    // the final row tau) raises the storage threshold.
+    float sig = (tau == -INFINITY && n <= kCap) ? -INFINITY : tmin;
+    if (pub != 0u) sig = fmaxf(sig, fkey_inv(pub));
+    if (tid == 0 && tau != -INFINITY) atomicMax(&row_pub[r], fkey(tau));
 
-
-    // ---- pass B: fast exp sum (Kahan in fp32) and candidates >= tau.  Each
-    // warp appends to its own shared-memory queue (ballot + popc, no atomics);
-    // the queues are copied to the chunk's global slots at the end.
+    // ---- pass B: fast exp sum (Kahan in fp32) and the float4 that hold
+    // candidates (elements >= sig)
     const float mref = (m == -INFINITY) ? 0.f : m;
     const float a = A.a;
+    // fast terms 2^(x * a - zref) with zref = fp32(m * a); a chunk whose m * a
+    // leaves the fp32 range keeps the two-step form 2^((x - m) * a) (zref NaN)
+    const float zr = __fmul_rn(mref, a);
+    const bool zok = fabsf(zr) <= FLT_MAX;
+    const float zref = zok ? zr : __int_as_float(0x7fc00000);
     float s = 0.f, comp = 0.f;
-    int wc = 0;  // this warp's queue length (warp-uniform)
-    Cand* q = cq[warp];
-    const unsigned lt = (1u << lane) - 1u;
-    auto push = [&](bool p, float x, int idx) {
-      const unsigned b = __ballot_sync(kAll, p);
-      if (p) {
-        const int pos = wc + __popc(b & lt);
-        if (pos < kWarpCap) q[pos] = Cand{x, idx};
-      }
-      wc += __popc(b);
-    };
-    uint32_t cmask = 0;  // bit i: this thread's float4 of step i holds an element >= tau
-    auto step = [&](const float4 v, int j, int i, bool partial) {
-      float e0 = term_fast(v.x, mref, a), e1 = term_fast(v.y, mref, a);
-      float e2 = term_fast(v.z, mref, a), e3 = term_fast(v.w, mref, a);
-      if (partial) {  // padding past the row end contributes nothing
-        if (j >= n) e0 = 0.f;
-        if (j + 1 >= n) e1 = 0.f;
-        if (j + 2 >= n) e2 = 0.f;
-        if (j + 3 >= n) e3 = 0.f;
-      }
-      const float t = __fadd_rn(__fadd_rn(e0, e1), __fadd_rn(e2, e3));
+    uint32_t cmask = 0;  // bit i: this thread's float4 of step i holds an element >= sig
+    auto kahan = [&](float t) {
       const float y = __fsub_rn(t, comp);
       const float ss = __fadd_rn(s, y);
       comp = __fsub_rn(__fsub_rn(ss, s), y);
       s = ss;
-      const float v4 = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
-      cmask |= (uint32_t)(v4 >= sig) << i;
     };
-    if (n == kChunk) {
+    if (n == kChunk && zok) {
+      // hot loop: both pairs of a float4 in one paired fma each
+      const unsigned long long a2 = f2_pack(a, a), nz2 = f2_pack(-zref, -zref);
 #pragma unroll 4
       for (int i = 0; i < kIters; i++) {
-        const int qq = tid + i * kThreads;
-        step(t4[qq], 4 * qq, i, false);
+        const float4 v = t4[tid + i * kThreads];
+        const float2 z01 = f2_unpack(f2_fma(f2_pack(v.x, v.y), a2, nz2));
+        const float2 z23 = f2_unpack(f2_fma(f2_pack(v.z, v.w), a2, nz2));
+        const unsigned long long e01 = f2_pack(ex2_approx(z01.x), ex2_approx(z01.y));
+        const unsigned long long e23 = f2_pack(ex2_approx(z23.x), ex2_approx(z23.y));
+        const float2 t2 = f2_unpack(f2_add(e01, e23));
+        kahan(__fadd_rn(t2.x, t2.y));
+        cmask |= (uint32_t)(fmaxf(fmax3(v.x, v.y, v.z), v.w) >= sig) << i;
       }
     } else {
+      // partial chunk, or zref out of range: one element at a time
       for (int i = 0; i < kIters; i++) {
         const int qq = tid + i * kThreads;
-        step(t4[qq], 4 * qq, i, true);
+        const float4 v = t4[qq];
+        const int j = 4 * qq;
+        const float xs[4] = {v.x, v.y, v.z, v.w};
+        float e[4];
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+          e[l] = zok ? term_fast_z(xs[l], a, zref) : term_fast(xs[l], mref, a);
+          if (j + l >= n) e[l] = 0.f;  // padding past the row end contributes nothing
+        }
+        kahan(__fadd_rn(__fadd_rn(e[0], e[2]), __fadd_rn(e[1], e[3])));
+        cmask |= (uint32_t)(fmaxf(fmax3(v.x, v.y, v.z), v.w) >= sig) << i;
       }
     }
-    // candidates: only the flagged float4 are read again (about 1-2 rounds per warp)
-    while (__any_sync(kAll, cmask != 0)) {
-      const bool has = cmask != 0;
-      const int i = has ? __ffs(cmask) - 1 : 0;
+    // candidates: each flagged float4 appends its elements >= sig to the
+    // chunk's global list (slots from a shared counter; the list's order is
+    // free, the finalizer sorts)
+    Cand* dst = A.cands + ((int64_t)r * A.n_chunks + c) * kCap;
+    while (cmask) {
+      const int i = __ffs(cmask) - 1;
       cmask &= cmask - 1u;
       const int qq = tid + i * kThreads;
       const float4 v = t4[qq];
       const int j = 4 * qq, gj = c0 + j;
-      push(has && v.x >= sig && j < n, v.x, gj);
-      push(has && v.y >= sig && j + 1 < n, v.y, gj + 1);
-      push(has && v.z >= sig && j + 2 < n, v.z, gj + 2);
-      push(has && v.w >= sig && j + 3 < n, v.w, gj + 3);
+      const bool k0 = v.x >= sig && j < n, k1 = v.y >= sig && j + 1 < n;
+      const bool k2 = v.z >= sig && j + 2 < n, k3 = v.w >= sig && j + 3 < n;
+      int pos = atomicAdd(&q_cnt, (int)k0 + (int)k1 + (int)k2 + (int)k3);
+      if (k0) { if (pos < kCap) dst[pos] = Cand{v.x, gj}; pos++; }
+      if (k1) { if (pos < kCap) dst[pos] = Cand{v.y, gj + 1}; pos++; }
+      if (k2) { if (pos < kCap) dst[pos] = Cand{v.z, gj + 2}; pos++; }
+      if (k3 && pos < kCap) dst[pos] = Cand{v.w, gj + 3};
     }
     double ds = (double)s - (double)comp;
     ds = warp_sum(ds);
-    if (lane == 0) { w_sum[warp] = ds; w_cnt[warp] = wc; }
+    if (lane == 0) w_sum[warp] = ds;
     __syncthreads();
-    // queue offsets; a full queue makes the chunk count exceed kCap (overflow)
-    int off = 0, tot = 0, ovf = 0;
-#pragma unroll
-    for (int w = 0; w < kWarps; w++) {
-      const int cw = w_cnt[w];
-      if (w < warp) off += cw;
-      tot += cw;
-      ovf |= cw > kWarpCap;
-    }
-    Cand* dst = A.cands + ((int64_t)r * A.n_chunks + c) * kCap;
-    const int mine = min(wc, kWarpCap);
-    for (int jj = lane; jj < mine; jj += 32)
-      if (off + jj < kCap) dst[off + jj] = q[jj];
-    if (tid == 0) {
-      double S = 0.0;
-      for (int w = 0; w < kWarps; w++) S += w_sum[w];
-      ChunkStat st;
-      st.m = m; st.tau = tau; st.s = S; st.n_cand = ovf ? kCap + 1 : tot;
-      st.best_i = INT_MAX; st.best_v = m; st.sig = sig;
-      A.stats[(int64_t)r * A.n_chunks + c] = st;
+    if (warp == 0) {
+      const double S = warp_sum(lane < kWarps ? w_sum[lane] : 0.0);
+      if (lane == 0) {
+        ChunkStat st;
+        st.m = m; st.tau = tau; st.s = S; st.n_cand = min(q_cnt, kCap + 1);
+        st.best_i = INT_MAX; st.zref = zref; st.sig = sig;
+        A.stats[(int64_t)r * A.n_chunks + c] = st;
+      }
     }
   }
 
   // ---- the last chunk of the row to finish finalizes it (unless a separate
   // finalize kernel follows)
-  if (A.split_finalize) {
-    // let the finalize grid launch while the last chunks stream
+  if (MODE != kGreedy) {
+    // sampled rows: finalize_kernel follows; let it launch while the last
+    // chunks stream
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     return;
   }
@@ -756,16 +770,17 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
   if (is_last) {
     __threadfence();
     if (!(*((volatile int32_t*)A.status) & kStatusTimeout))
-      finalize_row<MODE>(A, r, *reinterpret_cast<FinSmem*>(dyn_smem));
+      finalize_row<kGreedy>(A, r, *reinterpret_cast<FinSmem*>(dyn_smem));
   }
 }
 
 // Row finalize as its own grid (one CTA per row), launched as a programmatic
 // dependent of sample_kernel: it waits for the whole stream grid's writes.
 template <int MODE>
-__global__ void __launch_bounds__(kThreads) finalize_kernel(const __grid_constant__ Args A) {
+__global__ void __launch_bounds__(kThreads, 2) finalize_kernel(const __grid_constant__ Args A) {
   extern __shared__ __align__(128) unsigned char fin_smem[];
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (threadIdx.x == 0) A.row_count[blockIdx.x] = 0;  // the row bound, for the next call
   if (*((volatile int32_t*)A.status) & kStatusTimeout) return;
   finalize_row<MODE>(A, blockIdx.x, *reinterpret_cast<FinSmem*>(fin_smem));
 }
@@ -797,18 +812,22 @@ cudaError_t launch_mode(const Args& S, dim3 grid, cudaStream_t stream, cudaEvent
   sample_kernel<MODE, PEN><<<grid, dim3(kThreads), kSmem, stream>>>(S);
   cudaError_t e = cudaGetLastError();
   if (mid) cudaEventRecord(mid, stream);
-  if (e != cudaSuccess || !S.split_finalize) return e;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(S.B);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kFinSmem;
-  cfg.stream = stream;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  at[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = at;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, finalize_kernel<MODE>, S);
+  if constexpr (MODE == kGreedy) {
+    return e;  // the chunk kernel's last CTA of each row picks its id
+  } else {
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(S.B);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kFinSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, finalize_kernel<MODE>, S);
+  }
 }
 }  // namespace
 
@@ -816,7 +835,8 @@ cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev, i
   static bool attrs_done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attrs_done[dev]) {
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attrs_done[dev]) {
     cudaError_t e = cudaSuccess;
     if (e == cudaSuccess) e = set_attrs<kGreedy, false>();
     if (e == cudaSuccess) e = set_attrs<kGreedy, true>();
@@ -824,16 +844,16 @@ cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev, i
     if (e == cudaSuccess) e = set_attrs<kTopK, true>();
     if (e == cudaSuccess) e = set_attrs<kFull, false>();
     if (e == cudaSuccess) e = set_attrs<kFull, true>();
-    if (e == cudaSuccess) e = set_fin_attrs<kGreedy>();
     if (e == cudaSuccess) e = set_fin_attrs<kTopK>();
     if (e == cudaSuccess) e = set_fin_attrs<kFull>();
     if (e != cudaSuccess) return e;
     attrs_done[dev] = true;
   }
-  // rows in slices of at most 65535 (grid.y limit)
-  for (int64_t r0 = 0; r0 < A.B; r0 += 65535) {
+  // rows in slices small enough that row * n_chunks stays well inside int
+  const int64_t rmax = (INT_MAX - (1 << 20)) / A.n_chunks;
+  for (int64_t r0 = 0; r0 < A.B; r0 += rmax) {
     Args S = A;
-    const int rows = (int)((A.B - r0) < 65535 ? (A.B - r0) : 65535);
+    const int rows = (int)std::min<int64_t>(A.B - r0, rmax);
     S.B = rows;
     S.logits = A.logits + r0 * A.ld;
     if (A.hist_off) S.hist_off = A.hist_off + r0;
@@ -850,7 +870,7 @@ cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev, i
     if (A.d_row_sum) S.d_row_sum = A.d_row_sum + r0;
     if (A.d_total) S.d_total = A.d_total + r0;
     if (A.d_row_flags) S.d_row_flags = A.d_row_flags + r0;
-    const dim3 grid(A.n_chunks, rows);
+    const dim3 grid(rows, A.n_chunks);
     const bool pen = A.use_pen != 0;
     const bool prof = ev != nullptr && r0 == 0;
     if (prof) cudaEventRecord(ev[0], stream);
@@ -858,18 +878,21 @@ cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev, i
     cudaError_t e;
     switch (A.mode) {
       case kGreedy:
-        e = pen ? launch_mode<kGreedy, true>(S, grid, stream, mid) : launch_mode<kGreedy, false>(S, grid, stream, mid);
+        e = pen ? launch_mode<kGreedy, true>(S, grid, stream, mid)
+                : launch_mode<kGreedy, false>(S, grid, stream, mid);
         break;
       case kTopK:
-        e = pen ? launch_mode<kTopK, true>(S, grid, stream, mid) : launch_mode<kTopK, false>(S, grid, stream, mid);
+        e = pen ? launch_mode<kTopK, true>(S, grid, stream, mid)
+                : launch_mode<kTopK, false>(S, grid, stream, mid);
         break;
       default:
-        e = pen ? launch_mode<kFull, true>(S, grid, stream, mid) : launch_mode<kFull, false>(S, grid, stream, mid);
+        e = pen ? launch_mode<kFull, true>(S, grid, stream, mid)
+                : launch_mode<kFull, false>(S, grid, stream, mid);
         break;
     }
     if (prof) cudaEventRecord(ev[2], stream);
     if (e != cudaSuccess) return e;
-    if (launched) *launched += S.split_finalize ? 2 : 1;
+    if (launched) *launched += (A.mode == kGreedy) ? 1 : 2;
   }
   return cudaSuccess;
 }
