@@ -274,6 +274,7 @@ static int run_device(ms_ctx* ctx, DevState& s, const float* logits, int64_t B, 
   A.use_pen = P.use_pen;
   A.mode = P.mode;
   A.T = p->temperature;
+  A.rT = 1.0 / p->temperature;
   A.temper = P.temper;
   A.a = P.a;
   A.k = P.k;
@@ -536,6 +537,7 @@ extern "C" int ms_sample_noalloc(const float* logits, int64_t B, int64_t V, int6
   A.use_pen = P.use_pen;
   A.mode = P.mode;
   A.T = pp.temperature;
+  A.rT = 1.0 / pp.temperature;
   A.temper = P.temper;
   A.a = P.a;
   A.k = P.k;

@@ -60,6 +60,7 @@ struct Args {
   int32_t use_pen;
   int32_t mode;
   double T;              // temperature
+  double rT;             // fp64(1 / T)
   int32_t temper;        // 1 when T != 1.0
   float a;               // fp32(log2(e) / T): scale of the fast exp2 terms
   int32_t k;             // top_k as the reference uses it (0 = off)
@@ -110,6 +111,23 @@ __device__ __forceinline__ float pen_apply_fast(float v, double p, double rp) {
 
 __device__ __forceinline__ float temper_exact(float x, double T, int temper) {
   return temper ? __double2float_rn(__ddiv_rn((double)x, T)) : x;
+}
+
+// fp32(d / D) from q = d * rD (rD = fp64(1 / D)): q is within 3 fp64 ulps of
+// d / D, so both round to the same fp32 unless q lies next to an fp32
+// rounding midpoint (the 29 dropped bits read 1000...0), falls in the fp32
+// subnormal range, or is not finite; those take the exact divide.
+__device__ __forceinline__ float div_to_f32(double d, double D, double rD) {
+  const double q = __dmul_rn(d, rD);
+  const uint32_t low = (uint32_t)__double_as_longlong(q) & 0x1FFFFFFFu;
+  const double aq = fabs(q);
+  if ((uint32_t)(low - (0x10000000u - 16u)) <= 32u || (aq < 1.1754943508222875e-38 && aq != 0.0) ||
+      !(aq <= 1.7976931348623157e308))
+    return __double2float_rn(__ddiv_rn(d, D));
+  return __double2float_rn(q);
+}
+__device__ __forceinline__ float temper_fast(float x, double T, double rT, int temper) {
+  return temper ? div_to_f32((double)x, T, rT) : x;
 }
 
 __device__ __forceinline__ float term_exact(float xp, float mxp) {

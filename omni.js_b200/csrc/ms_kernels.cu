@@ -44,20 +44,17 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kFinChunks = 256;  // chunks whose scale the finalizer caches
 
 // =============================================================== shared scratch
-struct SelShared {  // kth_largest's radix state
-  int cnt[256];
-  int digit, rem;
-};
-
 // =============================================================== finalize
 struct FinSmem {
-  Cand gath[kGathMax];
-  unsigned long long keys[kFinMax];
-  SelShared sel;
+  Cand gath[kGathMax];              // candidates >= tau_row; later their sort keys
+  unsigned long long keys[kFinMax];  // the boundary bucket of the selection
+  unsigned long long top[kKmax];     // the selected top_k keys
+  int h1[256], h2[256];              // selection histograms
+  int b1, b2, need, n_lt, n_bkt, n_top;
   int nf, nF, slow, nan_row, overflow;
   unsigned long long corr;  // fixed-point (2^-50) sum of the candidate corrections
-  double S, S_fast, scale0;
-  float M, Mp, tau_row, xk, xlo;
+  double S, S_fast, scale0, u;
+  float M, Mp, tau_row, pout;
   float cm[kFinChunks];      // chunk maxima (first kFinChunks chunks)
   float cz[kFinChunks];      // their fast-term offsets
   double cs[kFinChunks];     // chunk_scale of each
@@ -68,7 +65,7 @@ __device__ __forceinline__ double chunk_scale(const Args& A, float mc, float zc,
   // reference's units.  2^(x*a - zref) = 2^((x - m_c)*a) * 2^(m_c*a - zref), so
   // 2^(zref - m_c*a) (the exponent is exact in fp64) undoes zref's rounding.
   if (mc == -INFINITY) return 0.0;
-  double sc = exp((double)mc / A.T - (double)Mp);
+  double sc = exp((double)mc * A.rT - (double)Mp);
   if (zc == zc) sc *= exp2((double)zc - (double)mc * (double)A.a);
   return sc;
 }
@@ -78,110 +75,102 @@ __device__ __forceinline__ float chunk_term(const Args& A, float x, float mc, fl
   return (zc == zc) ? term_fast_z(x, A.a, zc) : term_fast(x, mc, A.a);
 }
 
-// k-th largest x (1 <= k <= n) of the gathered candidates: radix select on
-// order-preserving keys, 8 bits per round.
-__device__ float kth_largest(const Cand* g, int n, int k, SelShared& sh) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  uint32_t prefix = 0, pmask = 0;
-  int rem = k;
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int d = tid; d < 256; d += kThreads) sh.cnt[d] = 0;
-    __syncthreads();
-    for (int j = tid; j < n; j += kThreads) {
-      const uint32_t key = fkey(g[j].x);
-      if ((key & pmask) == prefix) atomicAdd(&sh.cnt[(key >> shift) & 255], 1);
-    }
-    __syncthreads();
-    if (warp == 0) {
-      // lane l holds digits 255-8l .. 248-8l (descending)
-      int c[8], s = 0;
-#pragma unroll
-      for (int i = 0; i < 8; i++) { c[i] = sh.cnt[255 - 8 * lane - i]; s += c[i]; }
-      int incl = s;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t = __shfl_up_sync(kAll, incl, o);
-        if (lane >= o) incl += t;
-      }
-      const int excl = incl - s;
-      if (excl < rem && incl >= rem) {
-        int run = excl;
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-          if (run + c[i] >= rem) { sh.digit = 255 - 8 * lane - i; sh.rem = rem - run; break; }
-          run += c[i];
-        }
-      }
-    }
-    __syncthreads();
-    prefix |= (uint32_t)sh.digit << shift;
-    pmask |= 0xFFu << shift;
-    rem = sh.rem;
-    __syncthreads();
-  }
-  return fkey_inv(prefix);
-}
-
 __device__ __forceinline__ double key_prob(unsigned long long key) {
   return (double)__uint_as_float(0xFFFFFFFFu - (uint32_t)(key >> 32));
 }
 
+// Bucket of a 256-bin histogram (ascending) where the running count reaches
+// target (1 <= target <= total), and how many of that bucket's entries it
+// takes.  Called by one full warp.
+__device__ void scan_pick(const int* h, int target, int* bin_out, int* need_out) {
+  const int lane = threadIdx.x & 31;
+  int c[8], s = 0;
+#pragma unroll
+  for (int i = 0; i < 8; i++) { c[i] = h[8 * lane + i]; s += c[i]; }
+  int incl = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(kAll, incl, o);
+    if (lane >= o) incl += t;
+  }
+  const int excl = incl - s;
+  if (excl < target && incl >= target) {
+    int run = excl;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      if (run + c[i] >= target) { *bin_out = 8 * lane + i; *need_out = target - run; break; }
+      run += c[i];
+    }
+  }
+}
+
+// An fp32 probability p >= 2^-30 in units of 2^-53 (exact: its last bit is
+// worth at least 2^-53).
+__device__ __forceinline__ long long p_units(uint32_t pb) {
+  const int e = (int)(pb >> 23) - 127;
+  return (long long)((pb & 0x7FFFFFu) | 0x800000u) << (e + 30);
+}
+
 // Top-k, top-p and the draw over the first A.k sorted candidates
 // (src/generation.js:32-48), called by one full warp.  The reference sums in
-// fp64 sequentially.  When every probability is >= 2^-30 (a multiple of
-// 2^-53) and the k probabilities sum below 1, every partial sum is exact, so
-// the warp-parallel prefix sums, the cut and the draw equal the sequential
-// ones bit for bit; otherwise lane 0 runs the sequential loops.
-__device__ void topk_draw(const Args& A, int r, const unsigned long long* sorted, float Mp, double S,
+// fp64 sequentially.  When every probability is >= 2^-30 and the k
+// probabilities sum below 1, every partial sum is a multiple of 2^-53 below 1
+// and so exact in fp64: the sums are then done in integers (units of 2^-53),
+// in parallel, with the same results bit for bit.  The comparisons acc >= P
+// become units >= ceil(P * 2^53) (the scaling is exact).  Otherwise lane 0
+// runs the sequential loops.
+__device__ void topk_draw(const Args& A, int r, const unsigned long long* sorted, float Mp, double S, double u,
                           int* n_out) {
   const int lane = threadIdx.x & 31;
   const int k = A.k;
   const int per = (k + 31) / 32;
   const int i0 = min(k, lane * per), i1 = min(k, i0 + per);
-  double ls = 0.0;
+  long long ls = 0;
   bool ok = true;
   for (int i = i0; i < i1; i++) {
-    const double p = key_prob(sorted[i]);
-    ok &= p >= 9.313225746154785e-10;  // 2^-30
-    ls += p;
+    const uint32_t pb = 0xFFFFFFFFu - (uint32_t)(sorted[i] >> 32);
+    ok &= pb >= 0x30800000u && pb < 0x3F800000u;  // 2^-30 <= p < 1
+    if (ok) ls += p_units(pb);
   }
-  double incl = ls;
+  long long incl = ls;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const double t = __shfl_up_sync(kAll, incl, o);
+    const long long t = __shfl_up_sync(kAll, incl, o);
     if (lane >= o) incl += t;
   }
-  const double total_k = __shfl_sync(kAll, incl, 31);
-  const bool exact = __all_sync(kAll, ok) && total_k < 1.0;
-  const double u = A.u ? A.u[r] : 0.0;
+  const long long total_k = __shfl_sync(kAll, incl, 31);
+  const bool exact = __all_sync(kAll, ok) && total_k < (1ll << 53);
   int n = k, id = 0;
   double total = 0.0;
   if (exact) {
-    // first i with prefix_i >= target, or k when none
-    auto first_reach = [&](double target, int limit) {
-      double acc = incl - ls;
-      int hit = INT_MAX;
+    auto units = [&](int i) { return p_units(0xFFFFFFFFu - (uint32_t)(sorted[i] >> 32)); };
+    // first i < limit with prefix_i >= target, or UINT_MAX
+    auto first_reach = [&](long long target, int limit) {
+      long long acc = incl - ls;
+      unsigned hit = UINT_MAX;
       for (int i = i0; i < min(i1, limit); i++) {
-        acc += key_prob(sorted[i]);
-        if (acc >= target) { hit = i; break; }
+        acc += units(i);
+        if (acc >= target) { hit = (unsigned)i; break; }
       }
-      return __reduce_min_sync(kAll, (unsigned)hit);
+      return __reduce_min_sync(kAll, hit);
     };
-    if (A.use_topp) {
-      const unsigned h = first_reach(A.top_p, k);
-      n = (h == (unsigned)INT_MAX) ? k : (int)h + 1;
+    if (A.use_topp) {  // top_p < 1 here; below -1 it behaves as -1 (the first acc reaches it)
+      const unsigned h = first_reach((long long)ceil(fmax(A.top_p, -1.0) * 9007199254740992.0), k);
+      n = (h == UINT_MAX) ? k : (int)h + 1;
     }
     // total = prefix_{n-1}, held by the lane owning n-1
-    double acc = incl - ls, tot = 0.0;
+    long long acc = incl - ls, tot = 0;
     for (int i = i0; i < i1; i++) {
-      acc += key_prob(sorted[i]);
+      acc += units(i);
       if (i == n - 1) tot = acc;
     }
-    const int owner = (n - 1) / per;
-    total = __shfl_sync(kAll, tot, owner);
+    total = (double)__shfl_sync(kAll, tot, (n - 1) / per) * (1.0 / 9007199254740992.0);
     const double rr = u * total;
-    const unsigned h = first_reach(rr, n);
-    id = (int)(uint32_t)sorted[h == (unsigned)INT_MAX ? n - 1 : h];
+    // rr beyond every prefix (NaN, or u >= 1) draws the last candidate, as the
+    // reference's subtraction loop falls through
+    const long long rt = (rr <= 2.0) ? (long long)ceil(fmax(rr, -1.0) * 9007199254740992.0) : LLONG_MAX;
+    const unsigned h = first_reach(rt, n);
+    id = (int)(uint32_t)sorted[h == UINT_MAX ? n - 1 : h];
   } else if (lane == 0) {
     if (A.use_topp) {
       double a2 = 0.0;
@@ -266,7 +255,7 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
       nanr |= __shfl_xor_sync(kAll, nanr, o);
       ovf |= __shfl_xor_sync(kAll, ovf, o);
     }
-    const float Mp = temper_exact(M, A.T, A.temper);
+    const float Mp = temper_fast(M, A.T, A.rT, A.temper);
     if (M == -INFINITY || isinf(Mp) || Mp != Mp) nanr = 1;
     double S = 0.0;
     if (!nanr) {
@@ -282,8 +271,12 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
       F.M = M; F.Mp = Mp; F.tau_row = tr; F.nan_row = nanr; F.overflow = ovf;
       // a chunk that kept only elements >= sig > tau_row may miss candidates
       F.nf = 0; F.slow = ovf | (sg > tr); F.corr = 0ull; F.S_fast = S;
-      F.scale0 = nanr ? 0.0 : exp((double)M / A.T - (double)Mp);
+      F.scale0 = nanr ? 0.0 : exp((double)M * A.rT - (double)Mp);
     }
+  } else if (warp == 1) {
+    if (lane == 0) F.u = A.u ? __ldg(A.u + r) : 0.0;
+    for (int b = lane; b < 256; b += 32) { F.h1[b] = 0; F.h2[b] = 0; }
+    if (lane == 0) { F.n_top = 0; F.n_bkt = 0; }
   }
   __syncthreads();
   if (F.nan_row) {
@@ -306,78 +299,56 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   for (int c = warp; c < A.n_chunks; c += kWarps) {  // one chunk per warp at a time
     const int nc = min(__ldcg(&st[c].n_cand), kCap);
     const Cand* src = A.cands + ((int64_t)r * A.n_chunks + c) * kCap;
-    for (int j0 = 0; j0 < nc; j0 += 32) {
-      const int j = j0 + lane;
-      Cand cd;
-      cd.x = -INFINITY;
-      cd.i = 0;
-      if (j < nc) {
-        const float2 v = __ldcg(reinterpret_cast<const float2*>(src + j));
-        cd.x = v.x;
-        cd.i = __float_as_int(v.y);
+    for (int j0 = 0; j0 < nc; j0 += 128) {
+      float2 v[4];
+#pragma unroll
+      for (int t = 0; t < 4; t++) {  // four loads in flight per lane
+        const int j = j0 + 32 * t + lane;
+        v[t] = j < nc ? __ldcg(reinterpret_cast<const float2*>(src + j)) : make_float2(-INFINITY, 0.f);
       }
-      const bool keep = j < nc && cd.x >= tau_row;
-      const unsigned msk = __ballot_sync(kAll, keep);
-      if (msk) {
-        int base = 0;
-        if (lane == 0) base = atomicAdd(&F.nf, __popc(msk));
-        base = __shfl_sync(kAll, base, 0);
-        const int pos = base + __popc(msk & ((1u << lane) - 1u));
-        if (keep && pos < kGathMax) F.gath[pos] = cd;
+#pragma unroll
+      for (int t = 0; t < 4; t++) {
+        const int j = j0 + 32 * t + lane;
+        const bool keep = j < nc && v[t].x >= tau_row;
+        const unsigned msk = __ballot_sync(kAll, keep);
+        if (msk) {
+          int base = 0;
+          if (lane == 0) base = atomicAdd(&F.nf, __popc(msk));
+          base = __shfl_sync(kAll, base, 0);
+          const int pos = base + __popc(msk & ((1u << lane) - 1u));
+          if (keep && pos < kGathMax) F.gath[pos] = Cand{v[t].x, __float_as_int(v[t].y)};
+        }
       }
     }
   }
   __syncthreads();
   const int nf = F.nf;
-  const int ksum = (MODE == kTopK) ? A.k : min(A.ksum, nf);
-  if (nf > kGathMax || nf < ksum || ksum < 1) {
+  const int nfc = min(nf, kGathMax);
+  if (nf > kGathMax || (MODE == kTopK && nf < A.k)) {
     if (tid == 0) F.slow = 1;
   }
-  __syncthreads();
-  const int nfc = min(nf, kGathMax);
 
-  // ---- the ksum-th largest logit; exact terms of everything >= it correct the
-  // sum.  Those candidates are first compacted into a dense list (aliasing
-  // keys) so the fp64 work runs on full warps.
-  Cand* top = reinterpret_cast<Cand*>(F.keys);
-  if (!F.slow) {
-    const float xk = kth_largest(F.gath, nfc, ksum, F.sel);
-    if (tid == 0) { F.xk = xk; F.nF = 0; }
-    __syncthreads();
-    for (int j0 = warp * 32; j0 < nfc; j0 += kThreads) {
-      const int j = j0 + lane;
-      const Cand cd = j < nfc ? F.gath[j] : Cand{-INFINITY, 0};
-      const bool keep = j < nfc && cd.x >= xk;
-      const unsigned msk = __ballot_sync(kAll, keep);
-      if (msk) {
-        int base = 0;
-        if (lane == 0) base = atomicAdd(&F.nF, __popc(msk));
-        base = __shfl_sync(kAll, base, 0);
-        const int pos = base + __popc(msk & ((1u << lane) - 1u));
-        if (keep && pos < kFinMax) top[pos] = cd;
-      }
+  // ---- exact terms of every gathered candidate (kept in place of x) and the
+  // fast sum's correction: exact minus fast term, summed in 2^-50 units
+  {
+    long long corr = 0;
+    for (int j = tid; j < nfc; j += kThreads) {
+      Cand cd = F.gath[j];
+      const int c = cd.i / kChunk;
+      const float mc = c < kFinChunks ? F.cm[c] : __ldcg(&st[c].m);
+      const float zc = c < kFinChunks ? F.cz[c] : __ldcg(&st[c].zref);
+      const double sc = c < kFinChunks ? F.cs[c] : chunk_scale(A, mc, zc, Mp);
+      const float e = term_exact(temper_fast(cd.x, A.T, A.rT, A.temper), Mp);
+      corr += __double2ll_rn(((double)e - (double)chunk_term(A, cd.x, mc, zc) * sc) * 1125899906842624.0);
+      cd.x = e;
+      F.gath[j] = cd;
     }
-    __syncthreads();
-    const int ntop = F.nF;
-    if (ntop > kFinMax) {
-      if (tid == 0) F.slow = 1;
-    } else {
-      for (int j = tid; j < ntop; j += kThreads) {
-        const Cand cd = top[j];
-        const int c = cd.i / kChunk;
-        const float mc = c < kFinChunks ? F.cm[c] : __ldcg(&st[c].m);
-        const float zc = c < kFinChunks ? F.cz[c] : __ldcg(&st[c].zref);
-        const double sc = c < kFinChunks ? F.cs[c] : chunk_scale(A, mc, zc, Mp);
-        const float e = term_exact(temper_exact(cd.x, A.T, A.temper), Mp);
-        const double fast = (double)chunk_term(A, cd.x, mc, zc) * sc;
-        atomicAdd(&F.corr, (unsigned long long)__double2ll_rn(((double)e - fast) * 1125899906842624.0));  // 2^50
-      }
-    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) corr += __shfl_xor_sync(kAll, corr, o);
+    if (lane == 0 && corr != 0) atomicAdd(&F.corr, (unsigned long long)corr);
   }
   __syncthreads();
-  if (tid == 0) F.S = F.S_fast + (double)(long long)F.corr * (1.0 / 1125899906842624.0);
-  __syncthreads();
-  const double S = F.S;
+  const double S = F.S_fast + (double)(long long)F.corr * (1.0 / 1125899906842624.0);
 
   RowInfo R;
   R.row = A.logits + (int64_t)r * A.ld;
@@ -395,66 +366,82 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   R.nat16 = (float)(16.0 / A.T);
 
   if (MODE == kTopK && !F.slow) {
-    // Every element with prob == prob(x_k) must be in the list (x_lo >= tau_row).
-    // Usually the next fp32 value below x_k already has a smaller probability,
-    // so x_k is the low end of its tie group and no search is needed.
-    if (warp == 0) {
-      const float xk = F.xk;
-      bool search = false;
-      if (xk != -INFINITY) {
-        const float below = fkey_inv(fkey(xk) - 1u);
-        search = !(prob_of(R, below) < prob_of(R, xk));
+    const int k = A.k;
+    // ---- sort keys (prob desc, id asc) of the candidates, in place, and the
+    // histogram of their top byte
+    const double rS = 1.0 / S;
+    unsigned long long* key = reinterpret_cast<unsigned long long*>(F.gath);
+    for (int j = tid; j < nfc; j += kThreads) {
+      const Cand cd = F.gath[j];
+      const float p = div_to_f32((double)cd.x, S, rS);
+      const unsigned long long kk = ((unsigned long long)(0xFFFFFFFFu - __float_as_uint(p)) << 32) | (uint32_t)cd.i;
+      key[j] = kk;
+      atomicAdd(&F.h1[(int)(kk >> 56)], 1);
+    }
+    // every element outside the candidates has x < tau_row, so its probability
+    // is at most that of the fp32 value below tau_row
+    if (tid == 0) {
+      float po = -1.f;
+      if (tau_row != -INFINITY) {
+        const float below = fkey_inv(fkey(tau_row) - 1u);
+        po = div_to_f32((double)term_exact(temper_fast(below, A.T, A.rT, A.temper), Mp), S, rS);
       }
-      const float lo = search ? tie_low(R, xk) : xk;
-      if (lane == 0) {
-        F.xlo = lo;
-        if (lo < tau_row) F.slow = 1;
+      F.pout = po;
+    }
+    __syncthreads();
+    // ---- the k smallest keys: the k-th falls in bucket (b1, b2) of the keys'
+    // top 16 bits; what lies below it is in, and its own keys are ranked
+    if (warp == 0) scan_pick(F.h1, k, &F.b1, &F.need);
+    __syncthreads();
+    const uint32_t b1 = (uint32_t)F.b1;
+    for (int j = tid; j < nfc; j += kThreads) {
+      const unsigned long long kk = key[j];
+      if ((uint32_t)(kk >> 56) == b1) atomicAdd(&F.h2[(int)(kk >> 48) & 255], 1);
+    }
+    __syncthreads();
+    if (warp == 0) scan_pick(F.h2, F.need, &F.b2, &F.need);
+    __syncthreads();
+    const uint32_t p16 = (b1 << 8) | (uint32_t)F.b2;
+    const int need = F.need;  // keys of the bucket still to take (>= 1)
+    for (int j = tid; j < nfc; j += kThreads) {
+      const unsigned long long kk = key[j];
+      const uint32_t hi = (uint32_t)(kk >> 48);
+      if (hi < p16) {
+        const int q = atomicAdd(&F.n_top, 1);
+        if (q < kKmax) F.top[q] = kk;
+      } else if (hi == p16) {
+        const int q = atomicAdd(&F.n_bkt, 1);
+        if (q < kFinMax) F.keys[q] = kk;
       }
     }
     __syncthreads();
-    if (!F.slow) {
-      const float xlo = F.xlo;
-      auto key_of = [&](const Cand cd) {
-        const float p = prob_exact(term_exact(temper_exact(cd.x, A.T, A.temper), Mp), S);
-        return ((unsigned long long)(0xFFFFFFFFu - __float_as_uint(p)) << 32) | (uint32_t)cd.i;
-      };
-      if (xlo == F.xk) {
-        // the dense list is the candidate set: keys in place
-        const int ntop = F.nF;
-        for (int j = tid; j < ntop; j += kThreads) F.keys[j] = key_of(top[j]);
-      } else {
-        __syncthreads();
-        if (tid == 0) F.nF = 0;
-        __syncthreads();
-        for (int j0 = warp * 32; j0 < nfc; j0 += kThreads) {
-          const int j = j0 + lane;
-          const Cand cd = j < nfc ? F.gath[j] : Cand{-INFINITY, 0};
-          const bool keep = j < nfc && cd.x >= xlo;
-          const unsigned msk = __ballot_sync(kAll, keep);
-          if (msk) {
-            int base = 0;
-            if (lane == 0) base = atomicAdd(&F.nF, __popc(msk));
-            base = __shfl_sync(kAll, base, 0);
-            const int pos = base + __popc(msk & ((1u << lane) - 1u));
-            if (keep && pos < kFinMax) F.keys[pos] = key_of(cd);
-          }
+    const int nb = F.n_bkt;
+    if (nb <= kFinMax) {
+      for (int t = tid; t < nb; t += kThreads) {  // keys are distinct: the ids differ
+        const unsigned long long kk = F.keys[t];
+        int rank = 0;
+        for (int j = 0; j < nb; j++) rank += F.keys[j] < kk;
+        if (rank < need) {
+          const int q = atomicAdd(&F.n_top, 1);
+          if (q < kKmax) F.top[q] = kk;
         }
       }
+    }
+    __syncthreads();
+    if (nb <= kFinMax && F.n_top == k) {
+      // ---- the k keys in order (rank sort, into the bucket's space)
+      unsigned long long* sorted = F.keys;
+      for (int t = tid; t < k; t += kThreads) {
+        const unsigned long long kk = F.top[t];
+        int rank = 0;
+        for (int j = 0; j < k; j++) rank += F.top[j] < kk;
+        sorted[rank] = kk;
+      }
       __syncthreads();
-      const int nF = F.nF;
-      if (nF > kFinMax || nF < A.k) {
-        if (tid == 0) F.slow = 1;
-      } else {
-        // rank sort (keys are distinct: the low word is the id), into gath's space
-        unsigned long long* sorted = reinterpret_cast<unsigned long long*>(F.gath);
-        for (int t = tid; t < nF; t += kThreads) {
-          const unsigned long long key = F.keys[t];
-          int rank = 0;
-          for (int j = 0; j < nF; j++) rank += F.keys[j] < key;
-          sorted[rank] = key;
-        }
-        __syncthreads();
-        if (warp == 0) topk_draw(A, r, sorted, Mp, S, &F.nF);
+      // the k-th probability must beat every probability outside the
+      // candidates (else ties reach past them: rescan)
+      if (F.pout < (float)key_prob(sorted[k - 1])) {
+        if (warp == 0) topk_draw(A, r, sorted, Mp, S, F.u, &F.nF);
         __syncthreads();
         if (A.d_cand_ids || A.d_cand_probs) {
           const int n = F.nF;  // set by topk_draw
