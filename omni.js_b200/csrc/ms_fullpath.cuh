@@ -24,7 +24,7 @@ namespace ms {
 
 constexpr int kBins = 1024;      // buckets per refinement level
 constexpr int kExtCap = 1024;    // elements resolved exactly in shared memory
-constexpr int kFWarps = kThreads / 32;
+constexpr int kFWarps = kThreads / 32;  // most warps a row CTA has
 
 struct RowInfo {
   const float* row;
@@ -94,16 +94,16 @@ __device__ __forceinline__ void for_row(const RowInfo& R, F f) {
   if ((reinterpret_cast<uintptr_t>(R.row) & 15) == 0) {
     const int V4 = R.V >> 2;
     const float4* r4 = reinterpret_cast<const float4*>(R.row);
-    for (int q0 = tid; q0 < V4; q0 += 4 * kThreads) {
+    for (int q0 = tid; q0 < V4; q0 += 4 * (int)blockDim.x) {
       float4 v[4];
 #pragma unroll
       for (int u = 0; u < 4; u++) {
-        const int q = q0 + u * kThreads;
+        const int q = q0 + u * (int)blockDim.x;
         v[u] = q < V4 ? __ldg(r4 + q) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
       for (int u = 0; u < 4; u++) {
-        const int q = q0 + u * kThreads;
+        const int q = q0 + u * (int)blockDim.x;
         if (q >= V4) break;
         const int i = 4 * q;
         float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
@@ -119,9 +119,9 @@ __device__ __forceinline__ void for_row(const RowInfo& R, F f) {
         for (int t = 0; t < 4; t++) f(e[t], i + t);
       }
     }
-    for (int i = 4 * V4 + tid; i < R.V; i += kThreads) f(load_x(R, i), i);
+    for (int i = 4 * V4 + tid; i < R.V; i += (int)blockDim.x) f(load_x(R, i), i);
   } else {
-    for (int i = tid; i < R.V; i += kThreads) f(load_x(R, i), i);
+    for (int i = tid; i < R.V; i += (int)blockDim.x) f(load_x(R, i), i);
   }
 }
 
@@ -248,11 +248,18 @@ __device__ void warp_pick(const Hist& h, bool by_mass, double need, int* bin, lo
 }
 
 // Histogram of the elements that satisfy `in`, bucketed by `bin` (all threads).
+// Masses are summed exactly as integers in units of 2^-52 (a fast mass is at
+// most 1, the row's total about 1), with two 32-bit shared atomics per element
+// (the low word's returned old value gives the carry into the high word;
+// 64-bit shared atomics are emulated and far slower), and turned into doubles
+// at the end.
 template <typename In, typename Bin>
 __device__ void block_hist(const RowInfo& R, Hist& h, In in, Bin binf) {
-  for (int b = threadIdx.x; b < kBins; b += kThreads) {
+  uint32_t* mw = reinterpret_cast<uint32_t*>(h.mass);  // [2b] low word, [2b+1] high word
+  for (int b = threadIdx.x; b < kBins; b += (int)blockDim.x) {
     h.cnt[b] = 0;
-    h.mass[b] = 0.0;
+    mw[2 * b] = 0u;
+    mw[2 * b + 1] = 0u;
     h.kmin[b] = 0xFFFFFFFFu;
     h.kmax[b] = 0u;
   }
@@ -262,10 +269,20 @@ __device__ void block_hist(const RowInfo& R, Hist& h, In in, Bin binf) {
     const int b = binf(x);
     const uint32_t k = fkey(x);
     atomicAdd(&h.cnt[b], 1);
-    atomicAdd(&h.mass[b], mass_fast(R, x));
+    const unsigned long long m = (unsigned long long)__double2ll_rn(mass_fast(R, x) * 4503599627370496.0);
+    const uint32_t lo = (uint32_t)m, hi = (uint32_t)(m >> 32);
+    const uint32_t old = atomicAdd(&mw[2 * b], lo);
+    const uint32_t up = hi + (old + lo < old ? 1u : 0u);
+    if (up) atomicAdd(&mw[2 * b + 1], up);
     atomicMin(&h.kmin[b], k);
     atomicMax(&h.kmax[b], k);
   });
+  __syncthreads();
+  for (int b = threadIdx.x; b < kBins; b += (int)blockDim.x) {
+    // this thread alone reads the bucket's two words and writes the double over them
+    const double v = ((double)mw[2 * b + 1] * 4294967296.0 + (double)mw[2 * b]) * (1.0 / 4503599627370496.0);
+    h.mass[b] = v;
+  }
   __syncthreads();
 }
 
@@ -277,7 +294,7 @@ __device__ __forceinline__ long long block_sum_ll(long long v, FullSmem& sm) {
   if (lane == 0) sm.red_l[warp] = v;
   __syncthreads();
   long long t = 0;
-  for (int w = 0; w < kFWarps; w++) t += sm.red_l[w];
+  for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += sm.red_l[w];
   __syncthreads();
   return t;
 }
@@ -288,7 +305,7 @@ __device__ __forceinline__ double block_sum_d(double v, FullSmem& sm) {
   if (lane == 0) sm.red_d[warp] = v;
   __syncthreads();
   double t = 0.0;
-  for (int w = 0; w < kFWarps; w++) t += sm.red_d[w];
+  for (int w = 0; w < (int)(blockDim.x >> 5); w++) t += sm.red_d[w];
   __syncthreads();
   return t;
 }
@@ -297,7 +314,8 @@ __device__ __forceinline__ double block_sum_d(double v, FullSmem& sm) {
 // Warps own contiguous id ranges; the owner of the j-th scans its range.
 __device__ int index_select(const RowInfo& R, float glo, float ghi, long long j, FullSmem& sm) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int seg = (((R.V + kFWarps - 1) / kFWarps) + 31) & ~31;
+  const int nwarps = (int)(blockDim.x >> 5);
+  const int seg = (((R.V + nwarps - 1) / nwarps) + 31) & ~31;
   const int s0 = min(R.V, warp * seg), s1 = min(R.V, s0 + seg);
   int cnt = 0;
   for (int i = s0 + lane; i < s1; i += 32) {
@@ -450,11 +468,11 @@ __device__ FullSel select_full(const RowInfo& R, FullSmem& sm, bool by_mass, dou
   // ---- rank the middle exactly: bitonic sort of (prob desc, id asc) keys
   int np2 = 1;
   while (np2 < n_mid) np2 <<= 1;
-  for (int j = n_mid + tid; j < np2; j += kThreads) sm.key[j] = ~0ull;
+  for (int j = n_mid + tid; j < np2; j += (int)blockDim.x) sm.key[j] = ~0ull;
   __syncthreads();
   for (int kk = 2; kk <= np2; kk <<= 1) {
     for (int jj = kk >> 1; jj > 0; jj >>= 1) {
-      for (int i = tid; i < np2; i += kThreads) {
+      for (int i = tid; i < np2; i += (int)blockDim.x) {
         const int ixj = i ^ jj;
         if (ixj > i) {
           const unsigned long long x = sm.key[i], y = sm.key[ixj];
@@ -544,7 +562,7 @@ __device__ __forceinline__ void full_path(const Args& A, int r, const RowInfo& R
   const int V = R.V;
   block_hist(R, sm.h0, [](float) { return true; }, [&](float x) { return bin0(R, x); });
   double tm = 0.0;
-  for (int b = tid; b < kBins; b += kThreads) tm += sm.h0.mass[b];
+  for (int b = tid; b < kBins; b += (int)blockDim.x) tm += sm.h0.mass[b];
   const double total_all = block_sum_d(tm, sm);
   const bool use_k = A.k > 0 && A.k < V;
   long long n;

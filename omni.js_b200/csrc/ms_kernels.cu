@@ -203,6 +203,7 @@ __device__ void topk_draw(const Args& A, int r, const unsigned long long* sorted
 template <int MODE>
 __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nt = (int)blockDim.x, nw = nt >> 5;  // 256 or 512 threads
   const ChunkStat* st = A.stats + (int64_t)r * A.n_chunks;
   const int V = A.V;
 
@@ -296,7 +297,7 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   const float M = F.M, Mp = F.Mp, tau_row = F.tau_row;
 
   // ---- gather the candidates >= tau_row (all of them unless a chunk overflowed)
-  for (int c = warp; c < A.n_chunks; c += kWarps) {  // one chunk per warp at a time
+  for (int c = warp; c < A.n_chunks; c += nw) {  // one chunk per warp at a time
     const int nc = min(__ldcg(&st[c].n_cand), kCap);
     const Cand* src = A.cands + ((int64_t)r * A.n_chunks + c) * kCap;
     for (int j0 = 0; j0 < nc; j0 += 128) {
@@ -332,7 +333,7 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   // fast sum's correction: exact minus fast term, summed in 2^-50 units
   {
     long long corr = 0;
-    for (int j = tid; j < nfc; j += kThreads) {
+    for (int j = tid; j < nfc; j += nt) {
       Cand cd = F.gath[j];
       const int c = cd.i / kChunk;
       const float mc = c < kFinChunks ? F.cm[c] : __ldcg(&st[c].m);
@@ -371,7 +372,7 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
     // histogram of their top byte
     const double rS = 1.0 / S;
     unsigned long long* key = reinterpret_cast<unsigned long long*>(F.gath);
-    for (int j = tid; j < nfc; j += kThreads) {
+    for (int j = tid; j < nfc; j += nt) {
       const Cand cd = F.gath[j];
       const float p = div_to_f32((double)cd.x, S, rS);
       const unsigned long long kk = ((unsigned long long)(0xFFFFFFFFu - __float_as_uint(p)) << 32) | (uint32_t)cd.i;
@@ -394,7 +395,7 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
     if (warp == 0) scan_pick(F.h1, k, &F.b1, &F.need);
     __syncthreads();
     const uint32_t b1 = (uint32_t)F.b1;
-    for (int j = tid; j < nfc; j += kThreads) {
+    for (int j = tid; j < nfc; j += nt) {
       const unsigned long long kk = key[j];
       if ((uint32_t)(kk >> 56) == b1) atomicAdd(&F.h2[(int)(kk >> 48) & 255], 1);
     }
@@ -403,7 +404,7 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
     __syncthreads();
     const uint32_t p16 = (b1 << 8) | (uint32_t)F.b2;
     const int need = F.need;  // keys of the bucket still to take (>= 1)
-    for (int j = tid; j < nfc; j += kThreads) {
+    for (int j = tid; j < nfc; j += nt) {
       const unsigned long long kk = key[j];
       const uint32_t hi = (uint32_t)(kk >> 48);
       if (hi < p16) {
@@ -417,7 +418,7 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
     __syncthreads();
     const int nb = F.n_bkt;
     if (nb <= kFinMax) {
-      for (int t = tid; t < nb; t += kThreads) {  // keys are distinct: the ids differ
+      for (int t = tid; t < nb; t += nt) {  // keys are distinct: the ids differ
         const unsigned long long kk = F.keys[t];
         int rank = 0;
         for (int j = 0; j < nb; j++) rank += F.keys[j] < kk;
@@ -431,7 +432,7 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
     if (nb <= kFinMax && F.n_top == k) {
       // ---- the k keys in order (rank sort, into the bucket's space)
       unsigned long long* sorted = F.keys;
-      for (int t = tid; t < k; t += kThreads) {
+      for (int t = tid; t < k; t += nt) {
         const unsigned long long kk = F.top[t];
         int rank = 0;
         for (int j = 0; j < k; j++) rank += F.top[j] < kk;
@@ -445,7 +446,7 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
         __syncthreads();
         if (A.d_cand_ids || A.d_cand_probs) {
           const int n = F.nF;  // set by topk_draw
-          for (int i = tid; i < n && i < A.cand_cap; i += kThreads) {
+          for (int i = tid; i < n && i < A.cand_cap; i += nt) {
             const unsigned long long kkey = sorted[i];
             if (A.d_cand_ids) A.d_cand_ids[(int64_t)r * A.cand_cap + i] = (int32_t)(uint32_t)kkey;
             if (A.d_cand_probs)
@@ -462,10 +463,10 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   if (A.use_pen && A.penbits) {
     const int W = (V + 31) >> 5;
     uint32_t* pb = A.penbits + (int64_t)r * W;
-    for (int w = tid; w < W; w += kThreads) pb[w] = 0u;
+    for (int w = tid; w < W; w += nt) pb[w] = 0u;
     __syncthreads();
     const int64_t h0 = A.hist_off[r], h1 = A.hist_off[r + 1];
-    for (int64_t h = h0 + tid; h < h1; h += kThreads) {
+    for (int64_t h = h0 + tid; h < h1; h += nt) {
       const int id = A.hist[h];
       if (id >= 0 && id < V) atomicOr(&pb[id >> 5], 1u << (id & 31));
     }
@@ -763,8 +764,10 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
 
 // Row finalize as its own grid (one CTA per row), launched as a programmatic
 // dependent of sample_kernel: it waits for the whole stream grid's writes.
-template <int MODE>
-__global__ void __launch_bounds__(kThreads, 2) finalize_kernel(const __grid_constant__ Args A) {
+// NT threads per row: 512, or 256 for large top-k batches, whose rows then fit
+// one wave (4 CTAs per SM)
+template <int MODE, int NT>
+__global__ void __launch_bounds__(NT, kThreads * 2 / NT) finalize_kernel(const __grid_constant__ Args A) {
   extern __shared__ __align__(128) unsigned char fin_smem[];
   asm volatile("griddepcontrol.wait;" ::: "memory");
   if (threadIdx.x == 0) A.row_count[blockIdx.x] = 0;  // the row bound, for the next call
@@ -788,9 +791,9 @@ cudaError_t set_attrs() {
 
 constexpr size_t kFinSmem = sizeof(FullSmem) > sizeof(FinSmem) ? sizeof(FullSmem) : sizeof(FinSmem);
 
-template <int MODE>
+template <int MODE, int NT>
 cudaError_t set_fin_attrs() {
-  return cudaFuncSetAttribute((const void*)finalize_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  return cudaFuncSetAttribute((const void*)finalize_kernel<MODE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               (int)kFinSmem);
 }
 
@@ -805,7 +808,8 @@ cudaError_t launch_mode(const Args& S, dim3 grid, cudaStream_t stream, cudaEvent
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(S.B);
-    cfg.blockDim = dim3(kThreads);
+    const bool narrow = MODE == kTopK && S.B >= 256;
+    cfg.blockDim = dim3(narrow ? 256 : kThreads);
     cfg.dynamicSmemBytes = kFinSmem;
     cfg.stream = stream;
     cudaLaunchAttribute at[1];
@@ -813,7 +817,9 @@ cudaError_t launch_mode(const Args& S, dim3 grid, cudaStream_t stream, cudaEvent
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, finalize_kernel<MODE>, S);
+    if constexpr (MODE == kTopK)
+      if (narrow) return cudaLaunchKernelEx(&cfg, finalize_kernel<MODE, 256>, S);
+    return cudaLaunchKernelEx(&cfg, finalize_kernel<MODE, kThreads>, S);
   }
 }
 }  // namespace
@@ -831,8 +837,9 @@ cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev, i
     if (e == cudaSuccess) e = set_attrs<kTopK, true>();
     if (e == cudaSuccess) e = set_attrs<kFull, false>();
     if (e == cudaSuccess) e = set_attrs<kFull, true>();
-    if (e == cudaSuccess) e = set_fin_attrs<kTopK>();
-    if (e == cudaSuccess) e = set_fin_attrs<kFull>();
+    if (e == cudaSuccess) e = set_fin_attrs<kTopK, 256>();
+    if (e == cudaSuccess) e = set_fin_attrs<kTopK, kThreads>();
+    if (e == cudaSuccess) e = set_fin_attrs<kFull, kThreads>();
     if (e != cudaSuccess) return e;
     attrs_done[dev] = true;
   }
