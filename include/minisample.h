@@ -97,6 +97,8 @@ typedef struct ms_diag {
 #define MS_ROW_NAN       0x2   /* softmax produced NaN (NaN/+Inf logit, all -Inf row) */
 #define MS_ROW_FULLVOCAB 0x4   /* candidates ranked over the whole vocabulary        */
 #define MS_ROW_SLOWPATH  0x8   /* candidate set resolved by the exact row rescan     */
+#define MS_ROW_UNSETTLED 0x10  /* vocab-sharded merge: the shard lists cannot settle
+                                  the row (see ms_merge_records); out_ids gets -1    */
 
 typedef struct ms_ctx ms_ctx;
 
@@ -203,6 +205,41 @@ int ms_scratch_bytes(int64_t B, int64_t V, const ms_params* params, int64_t* out
 int ms_sample_noalloc(const float* logits, int64_t B, int64_t V, int64_t ld,
                       const int32_t* hist, const int64_t* hist_off, const ms_params* params,
                       const double* u, int32_t* out_ids, void* stream);
+
+/*
+ * Vocabulary sharding (one process and GPU per shard, the shards exchanging
+ * over NCCL).  No reference counterpart: the reference samples one whole row
+ * at a time.  GPU g holds columns [col0, col0 + cols) of every row.  A step is
+ *   1. ms_shard_records on every GPU: its shard of each row reduced to one
+ *      fixed-size record (rec_bytes from ms_shard_record_bytes): the shard's
+ *      penalised max, its fast softmax partial sum, and its candidates, which
+ *      are all its elements >= its k-th largest penalised logit (ties included);
+ *   2. the caller exchanges records so that the GPU merging a row holds that
+ *      row's record from every shard, in shard order (an all-to-all over rows);
+ *   3. ms_merge_records: per row, the global max and softmax sum, the exact
+ *      fp32 probabilities of the union of the candidates, top-k by
+ *      (prob desc, id asc), top-p and the draw - the same id as ms_sample on the
+ *      whole row, because the global top-k lies inside that union.
+ * Supported: greedy rows and 0 < top_k <= 256.  A row whose candidates cannot
+ * be proven sufficient (a shard's tie group at its k-th value too large, or a
+ * probability outside the union tying with the k-th) gets out_ids -1 and
+ * MS_ROW_UNSETTLED in diag->row_flags; the caller samples it from the whole row.
+ *
+ *   ms_shard_record_bytes  record size per row for these params
+ *   ms_shard_records       logits: [B, ld] fp32 device pointer to the shard's
+ *                          first column; hist/hist_off as for ms_sample (global
+ *                          ids); records: [B, rec_bytes] device buffer
+ *   ms_merge_records       records: [B, G, rec_bytes] device buffer (row-major,
+ *                          then shard); u, out_ids [B] device pointers
+ * Both run on `stream` (NULL = the ctx stream) on the context's first device.
+ */
+int ms_shard_record_bytes(int64_t V, const ms_params* params, int64_t* rec_bytes);
+int ms_shard_records(ms_ctx* ctx, const float* logits, int64_t B, int64_t V, int64_t col0, int64_t cols,
+                     int64_t ld, const int32_t* hist, const int64_t* hist_off, const ms_params* params,
+                     void* records, int64_t rec_bytes, void* stream);
+int ms_merge_records(ms_ctx* ctx, const void* records, int64_t B, int64_t G, int64_t V,
+                     const ms_params* params, const double* u, int32_t* out_ids, ms_diag* diag,
+                     int64_t rec_bytes, void* stream);
 
 #ifdef __cplusplus
 }

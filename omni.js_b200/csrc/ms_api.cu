@@ -15,6 +15,8 @@
 
 namespace ms {
 cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev, int64_t* launched);
+cudaError_t launch_shard(const Args& A, cudaStream_t stream);
+cudaError_t launch_merge(const Args& A, cudaStream_t stream);
 size_t finalize_smem_bytes();
 }  // namespace ms
 
@@ -73,6 +75,27 @@ Plan make_plan(int64_t V, const ms_params* p, bool have_hist) {
   if (P.kw < 1) P.kw = 1;
   if (P.kw > 32) P.kw = 32;
   return P;
+}
+
+// The Args fields that follow from the params and the plan.
+ms::Args param_args(const Plan& P, const ms_params* p) {
+  ms::Args A;
+  memset(&A, 0, sizeof A);
+  A.pen = p->repetition_penalty;
+  A.rpen = 1.0 / p->repetition_penalty;
+  A.use_pen = P.use_pen;
+  A.mode = P.mode;
+  A.T = p->temperature;
+  A.rT = 1.0 / p->temperature;
+  A.temper = P.temper;
+  A.a = P.a;
+  A.k = P.k;
+  A.kw = P.kw;
+  A.use_topp = P.use_topp;
+  A.top_p = p->top_p;
+  A.n_chunks = P.n_chunks;
+  A.ksum = ms::kKSum;
+  return A;
 }
 
 struct ScratchLayout {
@@ -554,5 +577,123 @@ extern "C" int ms_sample_noalloc(const float* logits, int64_t B, int64_t V, int6
   A.ksum = ms::kKSum;
   A.out_ids = out_ids;
   if (ms::launch_sample(A, st, nullptr, nullptr) != cudaSuccess) return MS_ERR_CUDA;
+  return MS_OK;
+}
+
+// ---------------------------------------------------------------- vocabulary shards
+namespace {
+// record bytes per row, or -1 when the params are not supported sharded
+int64_t record_bytes(int64_t V, const ms_params* p) {
+  const Plan P = make_plan(V, p, false);
+  if (P.mode == ms::kGreedy) return ms::kRecHead;
+  if (P.mode != ms::kTopK) return -1;
+  return ms::kRecHead + (int64_t)(P.k + ms::kTieSlack) * ms::kRecCand;
+}
+}  // namespace
+
+extern "C" int ms_shard_record_bytes(int64_t V, const ms_params* params, int64_t* rec_bytes) {
+  if (!params || !rec_bytes || V < 1) return MS_ERR_ARG;
+  const int64_t b = record_bytes(V, params);
+  if (b < 0) return MS_ERR_ARG;
+  *rec_bytes = b;
+  return MS_OK;
+}
+
+extern "C" int ms_shard_records(ms_ctx* ctx, const float* logits, int64_t B, int64_t V, int64_t col0, int64_t cols,
+                                int64_t ld, const int32_t* hist, const int64_t* hist_off, const ms_params* params,
+                                void* records, int64_t rec_bytes, void* stream) {
+  if (!ctx) return MS_ERR_ARG;
+  if (!params) return fail(ctx, MS_ERR_ARG, "ms_shard_records: params is NULL");
+  if (B < 0 || V < 1 || V > (int64_t)65535 * ms::kChunk || col0 < 0 || cols < 1 || col0 + cols > V || ld < cols)
+    return fail(ctx, MS_ERR_ARG, "ms_shard_records: bad B / V / col0 / cols / ld");
+  if (record_bytes(V, params) != rec_bytes)
+    return fail(ctx, MS_ERR_ARG, "ms_shard_records: rec_bytes differs from ms_shard_record_bytes (or top_k unsupported)");
+  if (B == 0) return MS_OK;
+  if (!logits || !records) return fail(ctx, MS_ERR_ARG, "ms_shard_records: logits/records is NULL");
+  if (hist_off != nullptr && hist == nullptr) return fail(ctx, MS_ERR_ARG, "ms_shard_records: hist_off without hist");
+  if (hist_off == nullptr) hist = nullptr;
+  DevState& s = ctx->devs[0];
+  MS_CUDA(ctx, cudaSetDevice(s.device));
+  cudaStream_t st = stream ? (cudaStream_t)stream : s.stream;
+  Plan P = make_plan(V, params, hist != nullptr);  // the mode and bound follow the whole row
+  P.n_chunks = (int)((cols + ms::kChunk - 1) / ms::kChunk);
+  if ((int64_t)B * P.n_chunks > (int64_t)INT32_MAX - (1 << 20))
+    return fail(ctx, MS_ERR_ARG, "ms_shard_records: B * chunks too large");
+  const ScratchLayout L = scratch_layout(B, cols, P);
+  int rc = ensure(ctx, &s.scratch, &s.scratch_bytes, L.total + (size_t)B * 4 + 256);
+  if (rc) return rc;
+  if (!s.status) {
+    MS_CUDA(ctx, cudaMalloc((void**)&s.status, 256));
+    MS_CUDA(ctx, cudaMemset(s.status, 0, 256));
+  }
+  if (s.counters_cap < B) {
+    if (s.counters) cudaFree(s.counters);
+    s.counters = nullptr;
+    s.counters_cap = 0;
+    const int64_t cap = B + B / 8 + 64;
+    MS_CUDA(ctx, cudaMalloc((void**)&s.counters, (size_t)cap * 4));
+    MS_CUDA(ctx, cudaMemset(s.counters, 0, (size_t)cap * 4));
+    s.counters_cap = cap;
+  }
+  char* base = (char*)s.scratch;
+  ms::Args A = param_args(P, params);
+  A.logits = logits;
+  A.ld = ld;
+  A.B = (int32_t)B;
+  A.V = (int32_t)cols;
+  A.col0 = (int32_t)col0;
+  A.hist = hist;
+  A.hist_off = hist_off;
+  A.stats = (ms::ChunkStat*)(base + L.stats);
+  A.cands = (ms::Cand*)(base + L.cands);
+  A.status = s.status;
+  A.row_count = s.counters;
+  A.out_ids = (int32_t*)(base + align_up(L.total, 256));  // greedy chunk kernel's per-shard ids (unused)
+  A.rec = (unsigned char*)records;
+  A.rec_bytes = (int32_t)rec_bytes;
+  A.k_send = (int32_t)((rec_bytes - ms::kRecHead) / ms::kRecCand);
+  MS_CUDA(ctx, ms::launch_shard(A, st));
+  s.launches += 2;
+  return MS_OK;
+}
+
+extern "C" int ms_merge_records(ms_ctx* ctx, const void* records, int64_t B, int64_t G, int64_t V,
+                                const ms_params* params, const double* u, int32_t* out_ids, ms_diag* diag,
+                                int64_t rec_bytes, void* stream) {
+  if (!ctx) return MS_ERR_ARG;
+  if (!params) return fail(ctx, MS_ERR_ARG, "ms_merge_records: params is NULL");
+  if (B < 0 || V < 1 || V > (int64_t)65535 * ms::kChunk || G < 1 || G > 32)
+    return fail(ctx, MS_ERR_ARG, "ms_merge_records: bad B / G / V (1 <= G <= 32)");
+  if (record_bytes(V, params) != rec_bytes)
+    return fail(ctx, MS_ERR_ARG, "ms_merge_records: rec_bytes differs from ms_shard_record_bytes (or top_k unsupported)");
+  const Plan P = make_plan(V, params, false);
+  if (P.mode == ms::kTopK && G * (int64_t)(P.k + ms::kTieSlack) > ms::kGathMax)
+    return fail(ctx, MS_ERR_ARG, "ms_merge_records: G * (top_k + 32) exceeds 4096 candidates");
+  if (B == 0) return MS_OK;
+  if (!records || !out_ids) return fail(ctx, MS_ERR_ARG, "ms_merge_records: records/out_ids is NULL");
+  if (P.mode != ms::kGreedy && !u) return fail(ctx, MS_ERR_ARG, "ms_merge_records: sampled rows need u[B]");
+  DevState& s = ctx->devs[0];
+  MS_CUDA(ctx, cudaSetDevice(s.device));
+  cudaStream_t st = stream ? (cudaStream_t)stream : s.stream;
+  ms::Args A = param_args(P, params);
+  A.B = (int32_t)B;
+  A.V = (int32_t)V;
+  A.u = u;
+  A.out_ids = out_ids;
+  A.rec = (unsigned char*)records;
+  A.rec_bytes = (int32_t)rec_bytes;
+  A.G = (int32_t)G;
+  if (diag) {
+    A.cand_cap = diag->cand_cap;
+    A.d_cand_ids = diag->cand_cap > 0 ? diag->cand_ids : nullptr;
+    A.d_cand_probs = diag->cand_cap > 0 ? diag->cand_probs : nullptr;
+    A.d_n_cand = diag->n_cand;
+    A.d_row_max = diag->row_max;
+    A.d_row_sum = diag->row_sum;
+    A.d_total = diag->total;
+    A.d_row_flags = diag->row_flags;
+  }
+  MS_CUDA(ctx, ms::launch_merge(A, st));
+  s.launches += 1;
   return MS_OK;
 }

@@ -29,6 +29,10 @@ constexpr int kGathMax = 4096;          // candidates >= the row threshold the f
 constexpr int kFinMax = 1024;           // candidates the finalizer ranks exactly
 constexpr int kKSum = 64;               // candidates kept for the sum correction when top_k is off
 
+constexpr int kRecHead = 32;             // vocab-shard record: header bytes
+constexpr int kRecCand = 16;             // bytes per listed candidate
+constexpr int kTieSlack = 32;            // list room beyond top_k for ties at a shard's k-th value
+
 // Status bits written by kernels (host maps them to MS_ERR_*).
 constexpr int kStatusTimeout = 0x1;
 
@@ -76,6 +80,12 @@ struct Args {
   uint32_t* penbits;     // [B, ceil(V/32)] penalty bitmap (slow path), may be null
   int32_t* out_ids;      // [B]
   int32_t* status;       // device status word
+  // vocabulary shards (0 / null otherwise)
+  int32_t col0;          // global column of local column 0 (penalty ids are global)
+  int32_t G;             // merge: shards per row
+  unsigned char* rec;    // shard records: [B, rec_bytes] (shard) or [B, G, rec_bytes] (merge)
+  int32_t rec_bytes;
+  int32_t k_send;        // shard: list capacity of a record
   // diagnostics (each may be null)
   int32_t cand_cap;
   int32_t* d_cand_ids;

@@ -51,7 +51,9 @@ struct FinSmem {
   unsigned long long top[kKmax];     // the selected top_k keys
   int h1[256], h2[256];              // selection histograms
   int b1, b2, need, n_lt, n_bkt, n_top;
-  int nf, nF, slow, nan_row, overflow;
+  int off[33];                       // merge: list offsets of the shards
+  uint32_t kx;                       // kth_largest_x: the selected key
+  int nf, nF, slow, nan_row, bad, overflow;
   unsigned long long corr;  // fixed-point (2^-50) sum of the candidate corrections
   double S, S_fast, scale0, u;
   float M, Mp, tau_row, pout;
@@ -200,10 +202,192 @@ __device__ void topk_draw(const Args& A, int r, const unsigned long long* sorted
   }
 }
 
+// Top-k by (prob desc, id asc) over the nfc gathered candidates, whose x
+// already holds the exact softmax term, then top-p and the draw; the id goes
+// to A.out_ids[r].  Before the call F.pout holds the largest probability any
+// element outside the candidates can have (-1: there is none), and F.h1, F.h2,
+// F.n_top, F.n_bkt are zero; F.pout is read after the first barrier here.
+// Returns false, with nothing written, when the candidates cannot settle the
+// row (a probability outside them could tie with the k-th).
+__device__ bool topk_from_terms(const Args& A, int r, FinSmem& F, int nfc, double S, double rS, float Mp) {
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int nt = (int)blockDim.x;
+  const int k = A.k;
+  // ---- sort keys (prob desc, id asc) of the candidates, in place, and the
+  // histogram of their top byte
+  unsigned long long* key = reinterpret_cast<unsigned long long*>(F.gath);
+  for (int j = tid; j < nfc; j += nt) {
+    const Cand cd = F.gath[j];
+    const float p = div_to_f32((double)cd.x, S, rS);
+    const unsigned long long kk = ((unsigned long long)(0xFFFFFFFFu - __float_as_uint(p)) << 32) | (uint32_t)cd.i;
+    key[j] = kk;
+    atomicAdd(&F.h1[(int)(kk >> 56)], 1);
+  }
+  __syncthreads();
+  // ---- the k smallest keys: the k-th falls in bucket (b1, b2) of the keys'
+  // top 16 bits; what lies below it is in, and its own keys are ranked
+  if (warp == 0) scan_pick(F.h1, k, &F.b1, &F.need);
+  __syncthreads();
+  const uint32_t b1 = (uint32_t)F.b1;
+  for (int j = tid; j < nfc; j += nt) {
+    const unsigned long long kk = key[j];
+    if ((uint32_t)(kk >> 56) == b1) atomicAdd(&F.h2[(int)(kk >> 48) & 255], 1);
+  }
+  __syncthreads();
+  if (warp == 0) scan_pick(F.h2, F.need, &F.b2, &F.need);
+  __syncthreads();
+  const uint32_t p16 = (b1 << 8) | (uint32_t)F.b2;
+  const int need = F.need;  // keys of the bucket still to take (>= 1)
+  for (int j = tid; j < nfc; j += nt) {
+    const unsigned long long kk = key[j];
+    const uint32_t hi = (uint32_t)(kk >> 48);
+    if (hi < p16) {
+      const int q = atomicAdd(&F.n_top, 1);
+      if (q < kKmax) F.top[q] = kk;
+    } else if (hi == p16) {
+      const int q = atomicAdd(&F.n_bkt, 1);
+      if (q < kFinMax) F.keys[q] = kk;
+    }
+  }
+  __syncthreads();
+  const int nb = F.n_bkt;
+  if (nb <= kFinMax) {
+    for (int t = tid; t < nb; t += nt) {  // keys are distinct: the ids differ
+      const unsigned long long kk = F.keys[t];
+      int rank = 0;
+      for (int j = 0; j < nb; j++) rank += F.keys[j] < kk;
+      if (rank < need) {
+        const int q = atomicAdd(&F.n_top, 1);
+        if (q < kKmax) F.top[q] = kk;
+      }
+    }
+  }
+  __syncthreads();
+  if (nb <= kFinMax && F.n_top == k) {
+    // ---- the k keys in order (rank sort, into the bucket's space)
+    unsigned long long* sorted = F.keys;
+    for (int t = tid; t < k; t += nt) {
+      const unsigned long long kk = F.top[t];
+      int rank = 0;
+      for (int j = 0; j < k; j++) rank += F.top[j] < kk;
+      sorted[rank] = kk;
+    }
+    __syncthreads();
+    // the k-th probability must beat every probability outside the
+    // candidates (else ties reach past them: rescan)
+    if (F.pout < (float)key_prob(sorted[k - 1])) {
+      if (warp == 0) topk_draw(A, r, sorted, Mp, S, F.u, &F.nF);
+      __syncthreads();
+      if (A.d_cand_ids || A.d_cand_probs) {
+        const int n = F.nF;  // set by topk_draw
+        for (int i = tid; i < n && i < A.cand_cap; i += nt) {
+          const unsigned long long kkey = sorted[i];
+          if (A.d_cand_ids) A.d_cand_ids[(int64_t)r * A.cand_cap + i] = (int32_t)(uint32_t)kkey;
+          if (A.d_cand_probs)
+            A.d_cand_probs[(int64_t)r * A.cand_cap + i] = __uint_as_float(0xFFFFFFFFu - (uint32_t)(kkey >> 32));
+        }
+      }
+      return true;
+    }
+  }
+  __syncthreads();
+  return false;
+}
+
+// Row statistics from the chunk stats (warp 0): max, tempered max, tau_row,
+// NaN and overflow flags, fast sum in units of exp(x' - Mp), chunk scales;
+// warp 1 prefetches u and clears the selection state.  Ends with a barrier.
+__device__ void row_stats(const Args& A, int r, FinSmem& F) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const ChunkStat* st = A.stats + (int64_t)r * A.n_chunks;
+  if (warp == 0) {
+    float M = -INFINITY, tr = -INFINITY, sg = -INFINITY;
+    int nanr = 0, ovf = 0;
+    for (int c = lane; c < A.n_chunks; c += 32) {
+      const float m = __ldcg(&st[c].m), t = __ldcg(&st[c].tau);
+      const double s = __ldcg(&st[c].s);
+      M = fmaxf(M, m);
+      tr = fmaxf(tr, t);
+      sg = fmaxf(sg, __ldcg(&st[c].sig));
+      nanr |= (s != s);
+      ovf |= (__ldcg(&st[c].n_cand) > kCap);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      M = fmaxf(M, __shfl_xor_sync(kAll, M, o));
+      tr = fmaxf(tr, __shfl_xor_sync(kAll, tr, o));
+      sg = fmaxf(sg, __shfl_xor_sync(kAll, sg, o));
+      nanr |= __shfl_xor_sync(kAll, nanr, o);
+      ovf |= __shfl_xor_sync(kAll, ovf, o);
+    }
+    const float Mp = temper_fast(M, A.T, A.rT, A.temper);
+    // a NaN, or a tempered max that is not finite, makes the softmax NaN; so
+    // does a row of -inf (the reference's exp(-inf - -inf))
+    const int bad = nanr | (Mp != Mp) | (isinf(Mp) && M != -INFINITY);
+    nanr = bad | (M == -INFINITY);
+    double S = 0.0;
+    if (!nanr) {
+      for (int c = lane; c < A.n_chunks; c += 32) {
+        const float m = __ldcg(&st[c].m), z = __ldcg(&st[c].zref);
+        const double sc = chunk_scale(A, m, z, Mp);
+        if (m != -INFINITY) S += __ldcg(&st[c].s) * sc;
+        if (c < kFinChunks) { F.cm[c] = m; F.cz[c] = z; F.cs[c] = sc; }
+      }
+      S = warp_sum(S);
+    }
+    if (lane == 0) {
+      F.M = M; F.Mp = Mp; F.tau_row = tr; F.nan_row = nanr; F.bad = bad; F.overflow = ovf;
+      // a chunk that kept only elements >= sig > tau_row may miss candidates
+      F.nf = 0; F.slow = ovf | (sg > tr); F.corr = 0ull; F.S_fast = S;
+      F.scale0 = nanr ? 0.0 : exp((double)M * A.rT - (double)Mp);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) F.u = A.u ? __ldg(A.u + r) : 0.0;
+    for (int b = lane; b < 256; b += 32) { F.h1[b] = 0; F.h2[b] = 0; }
+    if (lane == 0) { F.n_top = 0; F.n_bkt = 0; }
+  }
+  __syncthreads();
+}
+
+// Candidates >= tau_row of every chunk into F.gath (F.nf counts them, possibly
+// beyond kGathMax).  Ends with a barrier.
+__device__ void gather_cands(const Args& A, int r, FinSmem& F) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nw = (int)(blockDim.x >> 5);
+  const ChunkStat* st = A.stats + (int64_t)r * A.n_chunks;
+  const float tau_row = F.tau_row;
+  for (int c = warp; c < A.n_chunks; c += nw) {  // one chunk per warp at a time
+    const int nc = min(__ldcg(&st[c].n_cand), kCap);
+    const Cand* src = A.cands + ((int64_t)r * A.n_chunks + c) * kCap;
+    for (int j0 = 0; j0 < nc; j0 += 128) {
+      float2 v[4];
+#pragma unroll
+      for (int t = 0; t < 4; t++) {  // four loads in flight per lane
+        const int j = j0 + 32 * t + lane;
+        v[t] = j < nc ? __ldcg(reinterpret_cast<const float2*>(src + j)) : make_float2(-INFINITY, 0.f);
+      }
+#pragma unroll
+      for (int t = 0; t < 4; t++) {
+        const int j = j0 + 32 * t + lane;
+        const bool keep = j < nc && v[t].x >= tau_row;
+        const unsigned msk = __ballot_sync(kAll, keep);
+        if (msk) {
+          int base = 0;
+          if (lane == 0) base = atomicAdd(&F.nf, __popc(msk));
+          base = __shfl_sync(kAll, base, 0);
+          const int pos = base + __popc(msk & ((1u << lane) - 1u));
+          if (keep && pos < kGathMax) F.gath[pos] = Cand{v[t].x, __float_as_int(v[t].y)};
+        }
+      }
+    }
+  }
+  __syncthreads();
+}
+
 template <int MODE>
 __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nt = (int)blockDim.x, nw = nt >> 5;  // 256 or 512 threads
+  const int nt = (int)blockDim.x;  // 256 or 512 threads
   const ChunkStat* st = A.stats + (int64_t)r * A.n_chunks;
   const int V = A.V;
 
@@ -236,50 +420,7 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   }
 
   // ---- row max, NaN detection, overflow, tau_row, fast sum
-  if (warp == 0) {
-    float M = -INFINITY, tr = -INFINITY, sg = -INFINITY;
-    int nanr = 0, ovf = 0;
-    for (int c = lane; c < A.n_chunks; c += 32) {
-      const float m = __ldcg(&st[c].m), t = __ldcg(&st[c].tau);
-      const double s = __ldcg(&st[c].s);
-      M = fmaxf(M, m);
-      tr = fmaxf(tr, t);
-      sg = fmaxf(sg, __ldcg(&st[c].sig));
-      nanr |= (s != s);
-      ovf |= (__ldcg(&st[c].n_cand) > kCap);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      M = fmaxf(M, __shfl_xor_sync(kAll, M, o));
-      tr = fmaxf(tr, __shfl_xor_sync(kAll, tr, o));
-      sg = fmaxf(sg, __shfl_xor_sync(kAll, sg, o));
-      nanr |= __shfl_xor_sync(kAll, nanr, o);
-      ovf |= __shfl_xor_sync(kAll, ovf, o);
-    }
-    const float Mp = temper_fast(M, A.T, A.rT, A.temper);
-    if (M == -INFINITY || isinf(Mp) || Mp != Mp) nanr = 1;
-    double S = 0.0;
-    if (!nanr) {
-      for (int c = lane; c < A.n_chunks; c += 32) {
-        const float m = __ldcg(&st[c].m), z = __ldcg(&st[c].zref);
-        const double sc = chunk_scale(A, m, z, Mp);
-        if (m != -INFINITY) S += __ldcg(&st[c].s) * sc;
-        if (c < kFinChunks) { F.cm[c] = m; F.cz[c] = z; F.cs[c] = sc; }
-      }
-      S = warp_sum(S);
-    }
-    if (lane == 0) {
-      F.M = M; F.Mp = Mp; F.tau_row = tr; F.nan_row = nanr; F.overflow = ovf;
-      // a chunk that kept only elements >= sig > tau_row may miss candidates
-      F.nf = 0; F.slow = ovf | (sg > tr); F.corr = 0ull; F.S_fast = S;
-      F.scale0 = nanr ? 0.0 : exp((double)M * A.rT - (double)Mp);
-    }
-  } else if (warp == 1) {
-    if (lane == 0) F.u = A.u ? __ldg(A.u + r) : 0.0;
-    for (int b = lane; b < 256; b += 32) { F.h1[b] = 0; F.h2[b] = 0; }
-    if (lane == 0) { F.n_top = 0; F.n_bkt = 0; }
-  }
-  __syncthreads();
+  row_stats(A, r, F);
   if (F.nan_row) {
     // softmax is NaN everywhere: the stable sort keeps id order, no acc reaches
     // topP, r is NaN, and the draw loop falls through to the last candidate.
@@ -297,32 +438,7 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   const float M = F.M, Mp = F.Mp, tau_row = F.tau_row;
 
   // ---- gather the candidates >= tau_row (all of them unless a chunk overflowed)
-  for (int c = warp; c < A.n_chunks; c += nw) {  // one chunk per warp at a time
-    const int nc = min(__ldcg(&st[c].n_cand), kCap);
-    const Cand* src = A.cands + ((int64_t)r * A.n_chunks + c) * kCap;
-    for (int j0 = 0; j0 < nc; j0 += 128) {
-      float2 v[4];
-#pragma unroll
-      for (int t = 0; t < 4; t++) {  // four loads in flight per lane
-        const int j = j0 + 32 * t + lane;
-        v[t] = j < nc ? __ldcg(reinterpret_cast<const float2*>(src + j)) : make_float2(-INFINITY, 0.f);
-      }
-#pragma unroll
-      for (int t = 0; t < 4; t++) {
-        const int j = j0 + 32 * t + lane;
-        const bool keep = j < nc && v[t].x >= tau_row;
-        const unsigned msk = __ballot_sync(kAll, keep);
-        if (msk) {
-          int base = 0;
-          if (lane == 0) base = atomicAdd(&F.nf, __popc(msk));
-          base = __shfl_sync(kAll, base, 0);
-          const int pos = base + __popc(msk & ((1u << lane) - 1u));
-          if (keep && pos < kGathMax) F.gath[pos] = Cand{v[t].x, __float_as_int(v[t].y)};
-        }
-      }
-    }
-  }
-  __syncthreads();
+  gather_cands(A, r, F);
   const int nf = F.nf;
   const int nfc = min(nf, kGathMax);
   if (nf > kGathMax || (MODE == kTopK && nf < A.k)) {
@@ -367,20 +483,9 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   R.nat16 = (float)(16.0 / A.T);
 
   if (MODE == kTopK && !F.slow) {
-    const int k = A.k;
-    // ---- sort keys (prob desc, id asc) of the candidates, in place, and the
-    // histogram of their top byte
-    const double rS = 1.0 / S;
-    unsigned long long* key = reinterpret_cast<unsigned long long*>(F.gath);
-    for (int j = tid; j < nfc; j += nt) {
-      const Cand cd = F.gath[j];
-      const float p = div_to_f32((double)cd.x, S, rS);
-      const unsigned long long kk = ((unsigned long long)(0xFFFFFFFFu - __float_as_uint(p)) << 32) | (uint32_t)cd.i;
-      key[j] = kk;
-      atomicAdd(&F.h1[(int)(kk >> 56)], 1);
-    }
     // every element outside the candidates has x < tau_row, so its probability
     // is at most that of the fp32 value below tau_row
+    const double rS = 1.0 / S;
     if (tid == 0) {
       float po = -1.f;
       if (tau_row != -INFINITY) {
@@ -389,74 +494,7 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
       }
       F.pout = po;
     }
-    __syncthreads();
-    // ---- the k smallest keys: the k-th falls in bucket (b1, b2) of the keys'
-    // top 16 bits; what lies below it is in, and its own keys are ranked
-    if (warp == 0) scan_pick(F.h1, k, &F.b1, &F.need);
-    __syncthreads();
-    const uint32_t b1 = (uint32_t)F.b1;
-    for (int j = tid; j < nfc; j += nt) {
-      const unsigned long long kk = key[j];
-      if ((uint32_t)(kk >> 56) == b1) atomicAdd(&F.h2[(int)(kk >> 48) & 255], 1);
-    }
-    __syncthreads();
-    if (warp == 0) scan_pick(F.h2, F.need, &F.b2, &F.need);
-    __syncthreads();
-    const uint32_t p16 = (b1 << 8) | (uint32_t)F.b2;
-    const int need = F.need;  // keys of the bucket still to take (>= 1)
-    for (int j = tid; j < nfc; j += nt) {
-      const unsigned long long kk = key[j];
-      const uint32_t hi = (uint32_t)(kk >> 48);
-      if (hi < p16) {
-        const int q = atomicAdd(&F.n_top, 1);
-        if (q < kKmax) F.top[q] = kk;
-      } else if (hi == p16) {
-        const int q = atomicAdd(&F.n_bkt, 1);
-        if (q < kFinMax) F.keys[q] = kk;
-      }
-    }
-    __syncthreads();
-    const int nb = F.n_bkt;
-    if (nb <= kFinMax) {
-      for (int t = tid; t < nb; t += nt) {  // keys are distinct: the ids differ
-        const unsigned long long kk = F.keys[t];
-        int rank = 0;
-        for (int j = 0; j < nb; j++) rank += F.keys[j] < kk;
-        if (rank < need) {
-          const int q = atomicAdd(&F.n_top, 1);
-          if (q < kKmax) F.top[q] = kk;
-        }
-      }
-    }
-    __syncthreads();
-    if (nb <= kFinMax && F.n_top == k) {
-      // ---- the k keys in order (rank sort, into the bucket's space)
-      unsigned long long* sorted = F.keys;
-      for (int t = tid; t < k; t += nt) {
-        const unsigned long long kk = F.top[t];
-        int rank = 0;
-        for (int j = 0; j < k; j++) rank += F.top[j] < kk;
-        sorted[rank] = kk;
-      }
-      __syncthreads();
-      // the k-th probability must beat every probability outside the
-      // candidates (else ties reach past them: rescan)
-      if (F.pout < (float)key_prob(sorted[k - 1])) {
-        if (warp == 0) topk_draw(A, r, sorted, Mp, S, F.u, &F.nF);
-        __syncthreads();
-        if (A.d_cand_ids || A.d_cand_probs) {
-          const int n = F.nF;  // set by topk_draw
-          for (int i = tid; i < n && i < A.cand_cap; i += nt) {
-            const unsigned long long kkey = sorted[i];
-            if (A.d_cand_ids) A.d_cand_ids[(int64_t)r * A.cand_cap + i] = (int32_t)(uint32_t)kkey;
-            if (A.d_cand_probs)
-              A.d_cand_probs[(int64_t)r * A.cand_cap + i] = __uint_as_float(0xFFFFFFFFu - (uint32_t)(kkey >> 32));
-          }
-        }
-        return;
-      }
-    }
-    __syncthreads();
+    if (topk_from_terms(A, r, F, nfc, S, rS, Mp)) return;
   }
   // ---- exact rescan of the whole row
   const int flags = (MODE == kTopK) ? MS_ROW_SLOWPATH : 0;
@@ -545,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
       }
 #pragma unroll
       for (int q = 0; q < 4; q++) {
-        const uint32_t d = ids[q] - (uint32_t)c0;  // ids outside [c0, c0+n) wrap past n
+        const uint32_t d = ids[q] - (uint32_t)(A.col0 + c0);  // ids outside the chunk wrap past n
         if (d < (uint32_t)n) atomicOr(&penmask[d >> 5], 1u << (d & 31));
       }
     }
@@ -775,6 +813,298 @@ __global__ void __launch_bounds__(NT, kThreads * 2 / NT) finalize_kernel(const _
   finalize_row<MODE>(A, blockIdx.x, *reinterpret_cast<FinSmem*>(fin_smem));
 }
 
+// =============================================================== vocabulary shards
+// One record per row and shard: a header, then up to k_send candidates.
+struct ShardHead {
+  float M;         // max of the shard's penalised logits (-inf: none)
+  float t;         // every shard element with x >= t is in the list (-inf: the whole shard)
+  int32_t n;       // list length
+  int32_t flags;   // kRecBad: the softmax is NaN; kRecIncomplete: the list cannot be trusted
+  double S;        // fast softmax partial sum, in units of exp(x' - Mp_g), Mp_g = fp32(M / T)
+  int32_t best_i;  // greedy: global index of the shard's first max (INT_MAX: none)
+  int32_t x0nan;   // greedy: the shard holds column 0 and it is NaN
+};
+struct ShardCand {
+  float x;         // penalised logit
+  int32_t id;      // global id
+  double f;        // its fast term, in the header's S units
+};
+static_assert(sizeof(ShardHead) == 32 && sizeof(ShardCand) == 16, "shard record layout");
+constexpr int kRecBad = 1, kRecIncomplete = 2;
+static_assert(sizeof(ShardHead) == kRecHead && sizeof(ShardCand) == kRecCand, "record sizes");
+
+// The k-th largest x of the nfc gathered candidates (1 <= k <= nfc), ties
+// counted: two 8-bit digits of the order-preserving key pick its bucket, whose
+// members are ranked.  F.h1, F.h2, F.n_bkt are zero on entry.  NaN when the
+// bucket is too large to rank (the caller gives up on the row).
+__device__ float kth_largest_x(FinSmem& F, int nfc, int k) {
+  const int tid = threadIdx.x, warp = tid >> 5, nt = (int)blockDim.x;
+  // larger x first = ascending ~fkey(x)
+  for (int j = tid; j < nfc; j += nt) atomicAdd(&F.h1[~fkey(F.gath[j].x) >> 24], 1);
+  __syncthreads();
+  if (warp == 0) scan_pick(F.h1, k, &F.b1, &F.need);
+  __syncthreads();
+  const uint32_t b1 = (uint32_t)F.b1;
+  for (int j = tid; j < nfc; j += nt) {
+    const uint32_t key = ~fkey(F.gath[j].x);
+    if ((key >> 24) == b1) atomicAdd(&F.h2[(key >> 16) & 255], 1);
+  }
+  __syncthreads();
+  if (warp == 0) scan_pick(F.h2, F.need, &F.b2, &F.need);
+  __syncthreads();
+  const uint32_t p16 = (b1 << 8) | (uint32_t)F.b2;
+  const int need = F.need;
+  for (int j = tid; j < nfc; j += nt) {
+    const uint32_t key = ~fkey(F.gath[j].x);
+    if ((key >> 16) == p16) {
+      const int q = atomicAdd(&F.n_bkt, 1);
+      if (q < kFinMax) F.keys[q] = key;
+    }
+  }
+  __syncthreads();
+  const int nb = F.n_bkt;
+  if (nb > kFinMax) return __int_as_float(0x7fc00000);
+  // the need-th smallest key v of the bucket: #(< v) < need <= #(<= v)
+  for (int t = tid; t < nb; t += nt) {
+    const uint32_t kt = (uint32_t)F.keys[t];
+    int lt = 0, le = 0;
+    for (int j = 0; j < nb; j++) {
+      const uint32_t kj = (uint32_t)F.keys[j];
+      lt += kj < kt;
+      le += kj <= kt;
+    }
+    if (lt < need && le >= need) F.kx = kt;  // every writer writes the same value
+  }
+  __syncthreads();
+  return fkey_inv(~F.kx);
+}
+
+// softmax NaN everywhere (src/generation.js:9-17 with a NaN sum): the stable
+// sort keeps id order, no acc reaches topP, r is NaN, and the draw loop falls
+// through to the last candidate
+__device__ void nan_row_out(const Args& A, int r, float Mp) {
+  const bool use_k = A.k > 0 && A.k < A.V;
+  A.out_ids[r] = use_k ? A.k - 1 : A.V - 1;
+  if (A.d_n_cand) A.d_n_cand[r] = use_k ? A.k : A.V;
+  if (A.d_row_max) A.d_row_max[r] = (double)Mp;
+  if (A.d_row_sum) A.d_row_sum[r] = __longlong_as_double(0x7ff8000000000000ll);
+  if (A.d_total) A.d_total[r] = __longlong_as_double(0x7ff8000000000000ll);
+  if (A.d_row_flags) A.d_row_flags[r] = MS_ROW_NAN;
+}
+
+// Row records of one vocabulary shard (one CTA per row), a programmatic
+// dependent of the shard's chunk kernel.
+template <int MODE>
+__global__ void __launch_bounds__(256, 4) shard_kernel(const __grid_constant__ Args A) {
+  extern __shared__ __align__(128) unsigned char fin_smem[];
+  FinSmem& F = *reinterpret_cast<FinSmem*>(fin_smem);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nt = (int)blockDim.x;
+  const int r = blockIdx.x;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  ShardHead* H = reinterpret_cast<ShardHead*>(A.rec + (int64_t)r * A.rec_bytes);
+  ShardCand* L = reinterpret_cast<ShardCand*>(H + 1);
+  const ChunkStat* st = A.stats + (int64_t)r * A.n_chunks;
+  if (MODE == kGreedy) {
+    if (warp == 0) {
+      float bv = -INFINITY;
+      int bi = INT_MAX;
+      for (int c = lane; c < A.n_chunks; c += 32) {
+        const float v = __ldcg(&st[c].m);
+        const int i = __ldcg(&st[c].best_i);
+        if (v > bv || (v == bv && i < bi)) { bv = v; bi = i; }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(kAll, bv, o);
+        const int oi = __shfl_xor_sync(kAll, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      if (lane == 0) {
+        ShardHead h;
+        h.M = bv; h.t = -INFINITY; h.n = 0; h.flags = 0; h.S = 0.0;
+        h.best_i = (bv == -INFINITY || bi == INT_MAX) ? INT_MAX : A.col0 + bi;
+        const float x0 = A.logits[(int64_t)r * A.ld];
+        h.x0nan = (A.col0 == 0 && x0 != x0) ? 1 : 0;
+        *H = h;
+      }
+    }
+    return;
+  }
+  if (tid == 0) A.row_count[r] = 0;  // the row bound, for the next call
+  const int timed_out = *((volatile int32_t*)A.status) & kStatusTimeout;
+  row_stats(A, r, F);
+  if (F.nan_row || timed_out) {
+    if (tid == 0) {
+      ShardHead h;
+      h.M = F.M; h.t = -INFINITY; h.n = 0; h.S = 0.0; h.best_i = INT_MAX; h.x0nan = 0;
+      h.flags = timed_out ? kRecIncomplete : (F.bad ? kRecBad : 0);
+      *H = h;
+    }
+    return;
+  }
+  gather_cands(A, r, F);
+  const int nf = F.nf, nfc = min(nf, kGathMax);
+  bool incomplete = F.slow || nf > kGathMax;
+  float t = F.tau_row;  // all gathered: every element >= tau_row
+  if (!incomplete && nfc > A.k) {
+    t = kth_largest_x(F, nfc, A.k);
+    incomplete = (t != t);
+  }
+  if (tid == 0) F.n_top = 0;
+  __syncthreads();
+  if (!incomplete) {
+    for (int j = tid; j < nfc; j += nt) {
+      const Cand cd = F.gath[j];
+      if (cd.x >= t) {
+        const int q = atomicAdd(&F.n_top, 1);
+        if (q < A.k_send) {
+          const int c = cd.i / kChunk;
+          const float mc = c < kFinChunks ? F.cm[c] : __ldcg(&st[c].m);
+          const float zc = c < kFinChunks ? F.cz[c] : __ldcg(&st[c].zref);
+          const double sc = c < kFinChunks ? F.cs[c] : chunk_scale(A, mc, zc, F.Mp);
+          ShardCand e;
+          e.x = cd.x; e.id = A.col0 + cd.i; e.f = (double)chunk_term(A, cd.x, mc, zc) * sc;
+          L[q] = e;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const bool full = incomplete || F.n_top > A.k_send;
+    ShardHead h;
+    h.M = F.M; h.t = t; h.n = full ? 0 : F.n_top; h.flags = full ? kRecIncomplete : 0;
+    h.S = F.S_fast; h.best_i = INT_MAX; h.x0nan = 0;
+    *H = h;
+  }
+}
+
+// Merge of the G shard records of each row (one CTA per row).
+template <int MODE>
+__global__ void __launch_bounds__(256, 4) merge_kernel(const __grid_constant__ Args A) {
+  extern __shared__ __align__(128) unsigned char fin_smem[];
+  FinSmem& F = *reinterpret_cast<FinSmem*>(fin_smem);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nt = (int)blockDim.x;
+  const int r = blockIdx.x, G = A.G;
+  const unsigned char* base = A.rec + (int64_t)r * G * A.rec_bytes;
+  auto head = [&](int g) { return reinterpret_cast<const ShardHead*>(base + (int64_t)g * A.rec_bytes); };
+  auto unsettled = [&]() {
+    A.out_ids[r] = -1;
+    if (A.d_n_cand) A.d_n_cand[r] = 0;
+    if (A.d_row_flags) A.d_row_flags[r] = MS_ROW_UNSETTLED;
+  };
+  if (MODE == kGreedy) {
+    if (warp == 0) {
+      float bv = -INFINITY;
+      int bi = INT_MAX, x0n = 0;
+      for (int g = lane; g < G; g += 32) {
+        const ShardHead h = *head(g);
+        if (h.best_i != INT_MAX && (h.M > bv || (h.M == bv && h.best_i < bi))) { bv = h.M; bi = h.best_i; }
+        x0n |= h.x0nan;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(kAll, bv, o);
+        const int oi = __shfl_xor_sync(kAll, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        x0n |= __shfl_xor_sync(kAll, x0n, o);
+      }
+      if (lane == 0) {
+        // src/generation.js:51-55: a NaN at index 0 is never beaten
+        A.out_ids[r] = (x0n || bi == INT_MAX) ? 0 : bi;
+        if (A.d_row_flags) A.d_row_flags[r] = MS_ROW_GREEDY;
+        if (A.d_n_cand) A.d_n_cand[r] = 0;
+        if (A.d_row_max) A.d_row_max[r] = (double)bv;
+      }
+    }
+    return;
+  }
+  if (warp == 0) {
+    float M = -INFINITY;
+    int fl = 0, n = 0;
+    ShardHead h;
+    if (lane < G) {
+      h = *head(lane);
+      M = h.M;
+      fl = h.flags;
+      n = h.n;
+    }
+    float Mx = M;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      Mx = fmaxf(Mx, __shfl_xor_sync(kAll, Mx, o));
+      fl |= __shfl_xor_sync(kAll, fl, o);
+    }
+    const float Mp = temper_fast(Mx, A.T, A.rT, A.temper);
+    const int bad = (fl & kRecBad) | (Mp != Mp) | (isinf(Mp) && Mx != -INFINITY);
+    double S = 0.0, scale = 0.0;
+    if (lane < G && M != -INFINITY && !bad) {
+      scale = exp((double)temper_fast(M, A.T, A.rT, A.temper) - (double)Mp);
+      S = h.S * scale;
+    }
+    S = warp_sum(S);
+    int incl = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(kAll, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane < G) { F.off[lane] = incl - n; F.cs[lane] = scale; F.cm[lane] = h.t; }
+    if (lane == 31) F.nf = incl;
+    if (lane == 0) {
+      F.M = Mx; F.Mp = Mp; F.nan_row = bad | (Mx == -INFINITY); F.slow = (fl & kRecIncomplete) ? 1 : 0;
+      F.S_fast = S; F.corr = 0ull; F.u = A.u ? __ldg(A.u + r) : 0.0;
+    }
+  } else if (warp == 1) {
+    for (int b = lane; b < 256; b += 32) { F.h1[b] = 0; F.h2[b] = 0; }
+    if (lane == 0) { F.n_top = 0; F.n_bkt = 0; }
+  }
+  __syncthreads();
+  const float Mp = F.Mp;
+  if (F.nan_row) {
+    if (tid == 0) nan_row_out(A, r, Mp);
+    return;
+  }
+  const int nall = F.nf;
+  if (F.slow || nall > kGathMax || nall < A.k) {
+    if (tid == 0) unsettled();
+    return;
+  }
+  // exact terms of the union, and the correction of the fast sum
+  {
+    long long corr = 0;
+    for (int j = tid; j < nall; j += nt) {
+      int g = 0;
+      while (g + 1 < G && F.off[g + 1] <= j) g++;
+      const ShardCand* L = reinterpret_cast<const ShardCand*>(head(g) + 1);
+      const ShardCand c = L[j - F.off[g]];
+      const float e = term_exact(temper_fast(c.x, A.T, A.rT, A.temper), Mp);
+      corr += __double2ll_rn(((double)e - c.f * F.cs[g]) * 1125899906842624.0);
+      F.gath[j] = Cand{e, c.id};
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) corr += __shfl_xor_sync(kAll, corr, o);
+    if (lane == 0 && corr != 0) atomicAdd(&F.corr, (unsigned long long)corr);
+  }
+  __syncthreads();
+  const double S = F.S_fast + (double)(long long)F.corr * (1.0 / 1125899906842624.0);
+  const double rS = 1.0 / S;
+  // an element outside shard g's list has x < t_g
+  if (warp == 0) {
+    float po = -1.f;
+    if (lane < G) {
+      const float t = F.cm[lane];
+      if (t != -INFINITY)
+        po = div_to_f32((double)term_exact(temper_fast(fkey_inv(fkey(t) - 1u), A.T, A.rT, A.temper), Mp), S, rS);
+    }
+    po = warp_max(po);
+    if (lane == 0) F.pout = po;
+  }
+  if (!topk_from_terms(A, r, F, nall, S, rS, Mp)) {
+    if (tid == 0) unsettled();
+  }
+}
+
 static_assert(sizeof(FinSmem) <= kChunk * sizeof(float), "finalize scratch must fit in the chunk tile");
 static_assert(sizeof(FullSmem) <= kChunk * sizeof(float), "full-row scratch must fit in the chunk tile");
 static_assert(kChunk / 32 == kThreads, "one penalty bitmap word per thread");
@@ -823,6 +1153,67 @@ cudaError_t launch_mode(const Args& S, dim3 grid, cudaStream_t stream, cudaEvent
   }
 }
 }  // namespace
+
+namespace {
+constexpr size_t kShardSmem = sizeof(FinSmem);
+
+template <int MODE>
+cudaError_t launch_shard_mode(const Args& S, bool pen, cudaStream_t stream) {
+  const dim3 grid(S.B, S.n_chunks);
+  if (pen) sample_kernel<MODE, true><<<grid, dim3(kThreads), kSmem, stream>>>(S);
+  else sample_kernel<MODE, false><<<grid, dim3(kThreads), kSmem, stream>>>(S);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(S.B);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = kShardSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, shard_kernel<MODE>, S);
+}
+
+bool g_shard_attrs[64] = {false};
+cudaError_t shard_attrs(int dev) {
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (g_shard_attrs[dev]) return cudaSuccess;
+  cudaError_t e = cudaSuccess;
+  if (e == cudaSuccess) e = set_attrs<kGreedy, false>();
+  if (e == cudaSuccess) e = set_attrs<kGreedy, true>();
+  if (e == cudaSuccess) e = set_attrs<kTopK, false>();
+  if (e == cudaSuccess) e = set_attrs<kTopK, true>();
+  for (const void* f : {(const void*)shard_kernel<kGreedy>, (const void*)shard_kernel<kTopK>,
+                        (const void*)merge_kernel<kGreedy>, (const void*)merge_kernel<kTopK>})
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kShardSmem);
+  if (e == cudaSuccess) g_shard_attrs[dev] = true;
+  return e;
+}
+}  // namespace
+
+// Chunk kernel over a vocabulary shard, then its row records.
+cudaError_t launch_shard(const Args& A, cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t e = shard_attrs(dev);
+  if (e != cudaSuccess) return e;
+  return A.mode == kGreedy ? launch_shard_mode<kGreedy>(A, A.use_pen != 0, stream)
+                           : launch_shard_mode<kTopK>(A, A.use_pen != 0, stream);
+}
+
+// Merge of the shard records, one CTA per row.
+cudaError_t launch_merge(const Args& A, cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaError_t e = shard_attrs(dev);
+  if (e != cudaSuccess) return e;
+  if (A.mode == kGreedy) merge_kernel<kGreedy><<<dim3(A.B), dim3(256), kShardSmem, stream>>>(A);
+  else merge_kernel<kTopK><<<dim3(A.B), dim3(256), kShardSmem, stream>>>(A);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev, int64_t* launched) {
   static bool attrs_done[64] = {false};

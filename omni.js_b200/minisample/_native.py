@@ -32,6 +32,7 @@ MS_ROW_GREEDY = 0x1
 MS_ROW_NAN = 0x2
 MS_ROW_FULLVOCAB = 0x4
 MS_ROW_SLOWPATH = 0x8
+MS_ROW_UNSETTLED = 0x10
 
 ERROR_NAMES = {
     MS_ERR_ARG: "MS_ERR_ARG", MS_ERR_CUDA: "MS_ERR_CUDA", MS_ERR_NCCL: "MS_ERR_NCCL",
@@ -41,7 +42,8 @@ ERROR_NAMES = {
 
 # Every symbol include/minisample.h declares.
 EXPORTED = ("ms_version", "ms_create", "ms_destroy", "ms_last_error", "ms_sample", "ms_profile_read",
-            "ms_scratch_bytes", "ms_sample_noalloc", "ms_launch_count")
+            "ms_scratch_bytes", "ms_sample_noalloc", "ms_launch_count", "ms_shard_record_bytes",
+            "ms_shard_records", "ms_merge_records")
 
 
 class MsParams(ctypes.Structure):
@@ -104,6 +106,19 @@ def load(path: str | None = None):
     L.ms_profile_read.restype = ctypes.c_int
     L.ms_profile_read.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double),
                                   ctypes.POINTER(ctypes.c_int64)]
+    L.ms_shard_record_bytes.restype = ctypes.c_int
+    L.ms_shard_record_bytes.argtypes = [ctypes.c_int64, ctypes.POINTER(MsParams), ctypes.POINTER(ctypes.c_int64)]
+    L.ms_shard_records.restype = ctypes.c_int
+    L.ms_shard_records.argtypes = [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+        ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(MsParams), ctypes.c_void_p,
+        ctypes.c_int64, ctypes.c_void_p,
+    ]
+    L.ms_merge_records.restype = ctypes.c_int
+    L.ms_merge_records.argtypes = [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.POINTER(MsParams),
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(MsDiag), ctypes.c_int64, ctypes.c_void_p,
+    ]
     L.ms_launch_count.restype = ctypes.c_int
     L.ms_launch_count.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_int64)]
     L.ms_scratch_bytes.restype = ctypes.c_int

@@ -197,6 +197,82 @@ class Sampler:
         return ids
 
 
+    # ------------------------------------------------------------------ vocabulary shards
+    def shard_records(self, logits, V: int, col0: int, params: SampleParams, hist=None, hist_off=None,
+                      records=None, stream=None):
+        """Row records of one vocabulary shard: `logits` is the [B, cols] fp32 CUDA
+        view of columns [col0, col0 + cols) (row stride >= cols); hist / hist_off
+        hold global ids.  Returns a [B, rec_bytes] uint8 CUDA tensor."""
+        import torch
+
+        if logits.dtype != torch.float32 or logits.dim() != 2 or logits.stride(1) != 1:
+            raise ValueError("logits must be a [B, cols] float32 CUDA tensor with unit column stride")
+        B, cols = logits.shape
+        R = record_bytes(V, params)
+        if records is None:
+            records = torch.empty((B, R), dtype=torch.uint8, device=logits.device)
+        st = stream if stream is not None else torch.cuda.current_stream(logits.device)
+        p = params.to_c()
+        hp = hop = None
+        if hist_off is not None:
+            hp, hop = hist.data_ptr(), hist_off.data_ptr()
+        with torch.cuda.device(logits.device):
+            rc = self._L.ms_shard_records(self._ctx, logits.data_ptr(), B, V, col0, cols, logits.stride(0), hp, hop,
+                                          ctypes.byref(p), records.data_ptr(), R, ctypes.c_void_p(st.cuda_stream))
+        self._check(rc)
+        return records
+
+    def merge_records(self, records, V: int, params: SampleParams, u=None, out=None, diag: bool = False,
+                      cand_cap: int = 0, stream=None):
+        """Ids from the [B, G, rec_bytes] records of each row's G shards (in shard
+        order).  Unsettled rows get -1 (row flag MS_ROW_UNSETTLED)."""
+        import torch
+
+        B, G, R = records.shape
+        dev = records.device
+        ids = out if out is not None else torch.empty(B, dtype=torch.int32, device=dev)
+        D = keep = None
+        if diag:
+            keep = {
+                "n_cand": torch.zeros(B, dtype=torch.int32, device=dev),
+                "row_max": torch.zeros(B, dtype=torch.float64, device=dev),
+                "row_sum": torch.zeros(B, dtype=torch.float64, device=dev),
+                "total": torch.zeros(B, dtype=torch.float64, device=dev),
+                "row_flags": torch.zeros(B, dtype=torch.int32, device=dev),
+            }
+            D = N.MsDiag()
+            D.cand_cap = int(cand_cap)
+            if cand_cap > 0:
+                keep["cand_ids"] = torch.full((B, cand_cap), -1, dtype=torch.int32, device=dev)
+                keep["cand_probs"] = torch.zeros((B, cand_cap), dtype=torch.float32, device=dev)
+                D.cand_ids = keep["cand_ids"].data_ptr()
+                D.cand_probs = keep["cand_probs"].data_ptr()
+            for k in ("n_cand", "row_max", "row_sum", "total", "row_flags"):
+                setattr(D, k, keep[k].data_ptr())
+        st = stream if stream is not None else torch.cuda.current_stream(dev)
+        p = params.to_c()
+        with torch.cuda.device(dev):
+            rc = self._L.ms_merge_records(self._ctx, records.data_ptr(), B, G, V, ctypes.byref(p),
+                                          None if u is None else u.data_ptr(), ids.data_ptr(),
+                                          ctypes.byref(D) if D is not None else None, R,
+                                          ctypes.c_void_p(st.cuda_stream))
+        self._check(rc)
+        if diag:
+            return ids, keep
+        return ids
+
+
+def record_bytes(V: int, params: SampleParams) -> int:
+    """Bytes of one row's shard record (ms_shard_record_bytes)."""
+    L = N.load()
+    out = ctypes.c_int64()
+    p = params.to_c()
+    rc = L.ms_shard_record_bytes(V, ctypes.byref(p), ctypes.byref(out))
+    if rc != N.MS_OK:
+        raise N.MiniSampleError(rc, "ms_shard_record_bytes: these params are not supported vocab-sharded")
+    return out.value
+
+
 def scratch_bytes(B: int, V: int, params: SampleParams) -> int:
     L = N.load()
     out = ctypes.c_int64()
