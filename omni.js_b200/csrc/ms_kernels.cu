@@ -535,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
   __shared__ int w_bi[kWarps];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int r = blockIdx.x, c = blockIdx.y;  // chunk-major: a row's earlier chunks run first
+  const int r = blockIdx.x, c = blockIdx.y;  // rows vary fastest in launch order
   const int c0 = c * kChunk;
   const int n = min(kChunk, A.V - c0);
   const float* g = A.logits + (int64_t)r * A.ld + c0;
@@ -549,10 +549,6 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
   }
   if (PEN) penmask[tid] = 0u;  // kChunk / 32 == kThreads words
   if (tid == 0) q_cnt = 0;
-  // bound published by the row's chunks that ran earlier (0: none yet); the
-  // per-row counters serve sampled rows as this word, reset by the finalizer
-  uint32_t* row_pub = reinterpret_cast<uint32_t*>(A.row_count);
-  const uint32_t pub = (MODE != kGreedy) ? __ldcg(&row_pub[r]) : 0u;
   __syncthreads();
   if (bulk) {
     if (tid == 0) {
@@ -689,12 +685,8 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     const int n_ok = __popc(__ballot_sync(kAll, wok));
     const float tmin = n_ok ? fkey_inv(__reduce_min_sync(kAll, wok ? wk : 0xFFFFFFFFu)) : -INFINITY;
     const float tau = (n_ok * kwc >= keff) ? tmin : -INFINITY;
-    // A chunk too small for a bound keeps everything when it fits its list.
-    // The row bound that the row's earlier chunks published (pub, at most
-    // the final row tau) raises the storage threshold.
-    float sig = (tau == -INFINITY && n <= kCap) ? -INFINITY : tmin;
-    if (pub != 0u) sig = fmaxf(sig, fkey_inv(pub));
-    if (tid == 0 && tau != -INFINITY) atomicMax(&row_pub[r], fkey(tau));
+    // a chunk too small for a bound keeps everything when it fits its list
+    const float sig = (tau == -INFINITY && n <= kCap) ? -INFINITY : tmin;
 
     // ---- pass B: fast exp sum (Kahan in fp32) and the float4 that hold
     // candidates (elements >= sig)
@@ -808,7 +800,6 @@ template <int MODE, int NT>
 __global__ void __launch_bounds__(NT, kThreads * 2 / NT) finalize_kernel(const __grid_constant__ Args A) {
   extern __shared__ __align__(128) unsigned char fin_smem[];
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  if (threadIdx.x == 0) A.row_count[blockIdx.x] = 0;  // the row bound, for the next call
   if (*((volatile int32_t*)A.status) & kStatusTimeout) return;
   finalize_row<MODE>(A, blockIdx.x, *reinterpret_cast<FinSmem*>(fin_smem));
 }
@@ -930,7 +921,6 @@ __global__ void __launch_bounds__(256, 4) shard_kernel(const __grid_constant__ A
     }
     return;
   }
-  if (tid == 0) A.row_count[r] = 0;  // the row bound, for the next call
   const int timed_out = *((volatile int32_t*)A.status) & kStatusTimeout;
   row_stats(A, r, F);
   if (F.nan_row || timed_out) {
