@@ -29,6 +29,14 @@ class SampleParams:
                           float(self.top_p), float(self.repetition_penalty))
 
 
+def _stream_handle(st):
+    """The C ABI reads a NULL stream as the context's own stream.  torch's
+    default stream has handle 0 (CUDA's legacy default stream), so it is named
+    explicitly as cudaStreamLegacy (handle 1): the work then stays ordered with
+    the caller's other work on that stream."""
+    return ctypes.c_void_p(st.cuda_stream or 1)
+
+
 def _is_torch(x) -> bool:
     return type(x).__module__.startswith("torch")
 
@@ -190,7 +198,7 @@ class Sampler:
         with torch.cuda.device(dev):
             rc = self._L.ms_sample(self._ctx, logits.data_ptr(), B, V, ld, hp, hop, ctypes.byref(p), up,
                                    ids.data_ptr(), ctypes.byref(D) if D is not None else None, flags,
-                                   ctypes.c_void_p(st.cuda_stream))
+                                   _stream_handle(st))
         self._check(rc)
         if diag:
             return ids, keep
@@ -218,7 +226,7 @@ class Sampler:
             hp, hop = hist.data_ptr(), hist_off.data_ptr()
         with torch.cuda.device(logits.device):
             rc = self._L.ms_shard_records(self._ctx, logits.data_ptr(), B, V, col0, cols, logits.stride(0), hp, hop,
-                                          ctypes.byref(p), records.data_ptr(), R, ctypes.c_void_p(st.cuda_stream))
+                                          ctypes.byref(p), records.data_ptr(), R, _stream_handle(st))
         self._check(rc)
         return records
 
@@ -255,7 +263,7 @@ class Sampler:
             rc = self._L.ms_merge_records(self._ctx, records.data_ptr(), B, G, V, ctypes.byref(p),
                                           None if u is None else u.data_ptr(), ids.data_ptr(),
                                           ctypes.byref(D) if D is not None else None, R,
-                                          ctypes.c_void_p(st.cuda_stream))
+                                          _stream_handle(st))
         self._check(rc)
         if diag:
             return ids, keep

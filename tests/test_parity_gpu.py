@@ -275,3 +275,25 @@ def test_repeatable(sampler):
     a = sampler.sample(X, w.params, u=u, hist=hist, hist_off=off)
     b = sampler.sample(X, w.params, u=u, hist=hist, hist_off=off)
     np.testing.assert_array_equal(a, b)
+
+
+def test_default_stream_ordering(sampler):
+    """A device call on torch's default stream without MS_SYNC must stay ordered
+    with the next torch operation on that stream (the wrapper names the legacy
+    default stream explicitly; a NULL stream would mean the library's own)."""
+    import torch
+
+    from minisample import workloads as W
+
+    w = W.WORKLOADS["gemma_b512"]
+    dev = torch.device("cuda", 0)
+    x = W.logits_torch(w, 2, dev, B=256)
+    h, o = W.history_np(w, 2, B=256)
+    hd, od = torch.from_numpy(h).to(dev), torch.from_numpy(o).to(dev)
+    u = torch.from_numpy(W.uniforms(2, 256)).to(dev)
+    ref = sampler.sample(x, w.params, u=u, hist=hd, hist_off=od).clone()
+    for _ in range(3):
+        out = torch.full((256,), -1, dtype=torch.int32, device=dev)
+        sampler.sample(x, w.params, u=u, hist=hd, hist_off=od, out=out, sync=False)
+        got = out.clone()  # queued right behind the sampler's kernels
+        assert torch.equal(got, ref)
