@@ -54,8 +54,11 @@ def exchange_records(rec, group=None):
     world = dist.get_world_size(group)
     B, R = rec.shape
     Bb = -(-B // world)
-    send = torch.zeros((world * Bb, R), dtype=rec.dtype, device=rec.device)
-    send[:B] = rec
+    if world * Bb == B and rec.is_contiguous():
+        send = rec  # no padding rows needed
+    else:
+        send = torch.zeros((world * Bb, R), dtype=rec.dtype, device=rec.device)
+        send[:B] = rec
     recv = torch.empty_like(send)
     dist.all_to_all_single(recv, send, group=group)  # block s of recv: shard s's records of my rows
     return recv.view(world, Bb, R).permute(1, 0, 2).contiguous(), Bb
