@@ -144,3 +144,57 @@ async def generate_async(model, input_ids, options=None, rand=_random.random):
         return generated
     finally:
         model.dispose_cache(cache)
+
+
+def generate_tokens_batch(model, input_ids_batch, options=None, rands=None):
+    """B sequences at once: one sampler call per step over the rows still
+    running, each row with the rules of generate_tokens (the reference's
+    roadmap item of batched generation, README.md:232; per row
+    src/generation.js:97-114).  onToken(row, id, n) returning False stops that
+    row; EOS stops a row after it is appended.  rands[i] draws row i's
+    uniforms (one per sampled step of that row, none when greedy), so row i
+    gets the ids generate_tokens would give it with rands[i].  `model` is one
+    model for every row, or a list of one per row."""
+    opts = normalize_options(options)
+    B = len(input_ids_batch)
+    models = model if isinstance(model, (list, tuple)) else [model] * B
+    rands = rands if rands is not None else [_random.random] * B
+    on_token = opts["on_token"]
+    greedy = is_greedy(opts)
+    params = params_of(opts)
+    caches = [models[i].make_cache() for i in range(B)]
+    try:
+        generated = [[] for _ in range(B)]
+        last = [last_token_logits(models[i], input_ids_batch[i], caches[i]) for i in range(B)]
+        active = list(range(B))
+        for step in range(int(opts["max_new_tokens"])):
+            if not active:
+                break
+            X = np.ascontiguousarray(np.stack([last[i] for i in active]).astype(np.float32))
+            hs, offs = [], [0]
+            for i in active:
+                if generated[i]:  # the penalty starts once the row generated something
+                    h = np.asarray(list(input_ids_batch[i]) + generated[i], dtype=np.int64)
+                    hs.append(np.where((h < 0) | (h > 2**31 - 1), -1, h).astype(np.int32))
+                offs.append(offs[-1] + (hs[-1].shape[0] if generated[i] else 0))
+            hist = np.concatenate(hs) if hs else np.zeros(0, np.int32)
+            hist_off = np.asarray(offs, dtype=np.int64)
+            u = None if greedy else np.array([rands[i]() for i in active], dtype=np.float64)
+            ids = _sampler().sample(X, params, u=u, hist=hist, hist_off=hist_off)
+            still = []
+            for j, i in enumerate(active):
+                nid = int(ids[j])
+                generated[i].append(nid)
+                if on_token and on_token(i, nid, step + 1) is False:
+                    continue
+                if opts["eos_token_id"] is not None and nid == opts["eos_token_id"]:
+                    continue
+                still.append(i)
+            active = still
+            for i in active:
+                if step + 1 < int(opts["max_new_tokens"]):
+                    last[i] = last_token_logits(models[i], [generated[i][-1]], caches[i])
+        return generated
+    finally:
+        for i in range(B):
+            models[i].dispose_cache(caches[i])

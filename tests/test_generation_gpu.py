@@ -130,3 +130,32 @@ def test_generate_async_equals_sync(oracle):
     b = asyncio.run(generate_async(StubModel(3), [9, 9], dict(opts, tick=tick), rand=_mulberry(1)[0]))
     assert a == b
     assert len(ticks) == len(b) - 1 or len(ticks) == len(b)
+
+
+@pytest.mark.parametrize("case", [0, 1, 2])
+def test_generate_tokens_batch_matches_per_row(case):
+    """Row i of the batched loop equals generate_tokens on row i with the same
+    uniform stream; a row that hits EOS or onToken=false stops alone."""
+    from minisample.generation import generate_tokens, generate_tokens_batch, set_backend
+
+    set_backend("cuda")
+    opts = dict(CASES[case])
+    inputs = [[1, 2, 3], [7], [4, 4, 4, 4], [9, 8]]
+    per_row = [generate_tokens(StubModel(40 + i), inputs[i], opts, rand=_mulberry(60 + i)[0])
+               for i in range(len(inputs))]
+    eos = per_row[1][2]  # makes row 1 stop at its third id (and any other row that draws it)
+    stop_at = {3: 2}     # row 3 stops after its second id
+
+    def on_token(row, tid, n):
+        return not (row in stop_at and n >= stop_at[row])
+
+    opts_b = dict(opts, eosTokenId=eos, onToken=on_token)
+    got = generate_tokens_batch([StubModel(40 + i) for i in range(len(inputs))], inputs, opts_b,
+                                rands=[_mulberry(60 + i)[0] for i in range(len(inputs))])
+    for i in range(len(inputs)):
+        want = per_row[i]
+        if eos in want:
+            want = want[: want.index(eos) + 1]
+        if i in stop_at:
+            want = want[: stop_at[i]]
+        assert got[i] == want, (i, got[i], want)
