@@ -13,7 +13,7 @@
  *
  * The reference binds none of this natively: it calls the JS functions above.
  * The N-API shim (omni.js_b200/csrc/napi_minisample.c) turns
- * `addon.sample(...)` into `ms_sample` calls; INTEGRATION.md shows the JS side.
+ * `addon.sample(...)` into `ms_sample` calls.
  *
  * Conventions
  *   - Every entry point returns 0 on success or a negative MS_ERR_* code and
@@ -21,7 +21,16 @@
  *     to a CPU implementation.
  *   - The caller owns every buffer.  The logits are never modified (the
  *     reference copies them first, src/generation.js:72).
- *   - A context is used by one host thread at a time.
+ *   - A context is used by one host thread at a time.  Its scratch memory is
+ *     shared by every call made on it: two ms_sample calls whose kernels can
+ *     run at the same time (MS_DEVICE_PTRS calls on two streams with nothing
+ *     ordering them) race on that scratch.  Order such calls on one stream, or
+ *     give each stream its own context.
+ *   - Every bounded kernel wait that runs out marks its call as failed: the
+ *     rows of that call get id -1 (and MS_ROW_TIMEOUT in diag->row_flags).  A
+ *     synchronous call (MS_HOST_PTRS, or MS_DEVICE_PTRS | MS_SYNC) then returns
+ *     MS_ERR_TIMEOUT; an asynchronous device call reports it only through
+ *     those -1 ids.  A later call is not affected.
  */
 #ifndef MINISAMPLE_H
 #define MINISAMPLE_H
@@ -32,7 +41,7 @@
 extern "C" {
 #endif
 
-#define MS_ABI_VERSION 1
+#define MS_ABI_VERSION 2
 
 /* Error codes. */
 #define MS_OK            0
@@ -81,6 +90,10 @@ typedef struct ms_params {
  *   row_sum   [B]  softmax denominator sum(fp32(exp(x - max)))
  *   total     [B]  fp64 sum of the surviving candidates' probabilities
  *   row_flags [B]  MS_ROW_* bits below
+ *   pen_logits [B, pen_ld] fp32: every row after the repetition penalty and
+ *             before the temperature divide, i.e. the reference's `work` array
+ *             after src/generation.js:72-75 (pen_ld >= V; for MS_HOST_PTRS
+ *             calls, pen_ld is the stride of the host array)
  */
 typedef struct ms_diag {
     int32_t  cand_cap;
@@ -91,6 +104,8 @@ typedef struct ms_diag {
     double*  row_sum;
     double*  total;
     int32_t* row_flags;
+    float*   pen_logits;
+    int64_t  pen_ld;
 } ms_diag;
 
 #define MS_ROW_GREEDY    0x1   /* greedy argmax row                                  */
@@ -99,6 +114,7 @@ typedef struct ms_diag {
 #define MS_ROW_SLOWPATH  0x8   /* candidate set resolved by the exact row rescan     */
 #define MS_ROW_UNSETTLED 0x10  /* vocab-sharded merge: the shard lists cannot settle
                                   the row (see ms_merge_records); out_ids gets -1    */
+#define MS_ROW_TIMEOUT   0x20  /* a bounded wait of this call ran out; out_ids gets -1 */
 
 typedef struct ms_ctx ms_ctx;
 
@@ -175,6 +191,31 @@ int ms_launch_count(ms_ctx* ctx, int64_t* kernels);
 int ms_scratch_bytes(int64_t B, int64_t V, const ms_params* params, int64_t* out_bytes);
 
 /*
+ * Failure injection for testing the error paths; no reference counterpart.
+ * One-shot: the setting applies to the next ms_sample call on this context.
+ *   MS_INJECT_WAIT   the first chunk CTA of the next call waits `arg` (> 0)
+ *                    clock cycles on an mbarrier that nothing completes, so its
+ *                    bounded wait runs out: the call fails with MS_ERR_TIMEOUT
+ *                    (synchronous calls) and its ids are -1; nothing is in
+ *                    flight when the kernel returns
+ *   MS_INJECT_ALLOC  the next device allocation of the context fails as if
+ *                    cudaMalloc had, so the call returns MS_ERR_OOM
+ * arg 0 clears the setting.
+ */
+#define MS_INJECT_WAIT  1
+#define MS_INJECT_ALLOC 2
+int ms_debug_inject(ms_ctx* ctx, int what, int64_t arg);
+
+/*
+ * The double exp the sampler uses for exact softmax terms, fp32(exp(x' - mx))
+ * (src/generation.js:14), over n device doubles: y[i] = exp(x[i]) computed by
+ * fdlibm's published method, as V8's Math.exp does.  For testing that
+ * function against a host restatement; no reference counterpart.  Device
+ * pointers, on `stream` (NULL = default stream); asynchronous.
+ */
+int ms_debug_exp(const double* x, double* y, int64_t n, void* stream);
+
+/*
  * ms_sample without a context and without allocating.  No counterpart in the
  * reference: it exists for callers that cannot call cudaMalloc.  Examples are a
  * host program whose own allocator already reserved the device memory, or a
@@ -197,8 +238,9 @@ int ms_scratch_bytes(int64_t B, int64_t V, const ms_params* params, int64_t* out
  * before any stream capture.
  *
  * Returns MS_OK, MS_ERR_ARG, MS_ERR_SCRATCH, MS_ERR_STATE or MS_ERR_CUDA.  No
- * message is kept (there is no context).  A kernel wait that runs out is not
- * reported by this call.
+ * message is kept (there is no context).  The call returns before its kernels
+ * run, so a kernel wait that runs out is not in its return code: the rows of
+ * such a call come back as id -1.
  */
 #define MS_NOALLOC_SCRATCH_BYTES (8u << 20)
 #define MS_ERR_SCRATCH  -7   /* ms_sample_noalloc: the call needs more than MS_NOALLOC_SCRATCH_BYTES */

@@ -17,6 +17,7 @@ namespace ms {
 cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev, int64_t* launched);
 cudaError_t launch_shard(const Args& A, cudaStream_t stream);
 cudaError_t launch_merge(const Args& A, cudaStream_t stream);
+cudaError_t launch_exp(const double* x, double* y, int64_t n, cudaStream_t stream);
 size_t finalize_smem_bytes();
 }  // namespace ms
 
@@ -29,7 +30,9 @@ struct DevState {
   size_t scratch_bytes = 0;
   void* io = nullptr;       // device copies of host arguments
   size_t io_bytes = 0;
-  int32_t* status = nullptr;    // device status word (zeroed at creation and after a report)
+  int32_t* status = nullptr;    // device status word: the epoch of the last call whose wait ran out
+  int32_t epoch = 0;            // epoch of the last call launched on this device (never 0 once used)
+  std::vector<int64_t> host_offs;  // host staging of the rebased history offsets (lives until the call's sync)
   int32_t* counters = nullptr;  // per-row chunk counters; kernels leave them at zero
   int64_t counters_cap = 0;
   std::vector<std::array<cudaEvent_t, 3>> prof_pending;  // MS_PROFILE calls not yet read
@@ -120,6 +123,8 @@ ScratchLayout scratch_layout(int64_t B, int64_t V, const Plan& P) {
 struct ms_ctx {
   std::vector<DevState> devs;
   std::string err = "no error";
+  long long inject_wait = 0;   // ms_debug_inject(MS_INJECT_WAIT): cycles, next call only
+  bool inject_alloc = false;   // ms_debug_inject(MS_INJECT_ALLOC): fail the next allocation
 };
 
 static int fail(ms_ctx* c, int code, const char* fmt, ...) {
@@ -140,6 +145,18 @@ static int fail(ms_ctx* c, int code, const char* fmt, ...) {
                   #call, cudaGetErrorString(e_), __FILE__, __LINE__);                           \
   } while (0)
 
+// Every device allocation of a context goes through here (so a test can make
+// one fail, ms_debug_inject).
+static int dev_alloc(ms_ctx* ctx, void** p, size_t sz) {
+  if (ctx->inject_alloc) {
+    ctx->inject_alloc = false;
+    *p = nullptr;
+    return fail(ctx, MS_ERR_OOM, "cudaMalloc(%zu bytes): out of memory (injected)", sz);
+  }
+  MS_CUDA(ctx, cudaMalloc(p, sz));
+  return MS_OK;
+}
+
 static int ensure(ms_ctx* ctx, void** buf, size_t* have, size_t need) {
   if (*have >= need) return MS_OK;
   if (*buf) {
@@ -148,8 +165,44 @@ static int ensure(ms_ctx* ctx, void** buf, size_t* have, size_t need) {
     *have = 0;
   }
   size_t sz = need + need / 8;
-  MS_CUDA(ctx, cudaMalloc(buf, sz));
+  int rc = dev_alloc(ctx, buf, sz);
+  if (rc) return rc;
   *have = sz;
+  return MS_OK;
+}
+
+// The status word and the per-row counters of device state s (allocated once,
+// grown with B).
+static int ensure_state(ms_ctx* ctx, DevState& s, int64_t B) {
+  if (!s.status) {
+    int rc = dev_alloc(ctx, (void**)&s.status, 256);
+    if (rc) return rc;
+    MS_CUDA(ctx, cudaMemset(s.status, 0, 256));
+  }
+  if (s.counters_cap < B) {
+    if (s.counters) cudaFree(s.counters);
+    s.counters = nullptr;
+    s.counters_cap = 0;
+    const int64_t cap = B + B / 8 + 64;
+    int rc = dev_alloc(ctx, (void**)&s.counters, (size_t)cap * 4);
+    if (rc) return rc;
+    MS_CUDA(ctx, cudaMemset(s.counters, 0, (size_t)cap * 4));
+    s.counters_cap = cap;
+  }
+  return MS_OK;
+}
+
+static int32_t next_epoch(DevState& s) {
+  s.epoch = (s.epoch >= INT32_MAX - 1) ? 1 : s.epoch + 1;
+  return s.epoch;
+}
+
+// Did a wait of the call with this epoch run out?  (after a stream sync)
+static int read_status(ms_ctx* ctx, DevState& s, const char* who) {
+  int32_t status = 0;
+  cudaError_t e = cudaMemcpy(&status, s.status, sizeof status, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail(ctx, MS_ERR_CUDA, "%s: %s", who, cudaGetErrorString(e));
+  if (status == s.epoch) return fail(ctx, MS_ERR_TIMEOUT, "%s: a kernel wait timed out", who);
   return MS_OK;
 }
 
@@ -253,6 +306,20 @@ int ms_launch_count(ms_ctx* c, int64_t* kernels) {
   return MS_OK;
 }
 
+int ms_debug_inject(ms_ctx* c, int what, int64_t arg) {
+  if (!c || arg < 0) return MS_ERR_ARG;
+  if (what == MS_INJECT_WAIT) c->inject_wait = (long long)arg;
+  else if (what == MS_INJECT_ALLOC) c->inject_alloc = arg != 0;
+  else return fail(c, MS_ERR_ARG, "ms_debug_inject: unknown injection %d", what);
+  return MS_OK;
+}
+
+int ms_debug_exp(const double* x, double* y, int64_t n, void* stream) {
+  if (n < 0 || (n > 0 && (!x || !y))) return MS_ERR_ARG;
+  if (n == 0) return MS_OK;
+  return ms::launch_exp(x, y, n, (cudaStream_t)stream) == cudaSuccess ? MS_OK : MS_ERR_CUDA;
+}
+
 int ms_scratch_bytes(int64_t B, int64_t V, const ms_params* params, int64_t* out_bytes) {
   if (!params || !out_bytes || B < 0 || V < 1) return MS_ERR_ARG;
   const Plan P = make_plan(V, params, true);
@@ -270,19 +337,8 @@ static int run_device(ms_ctx* ctx, DevState& s, const float* logits, int64_t B, 
   const ScratchLayout L = scratch_layout(B, V, P);
   int rc = ensure(ctx, &s.scratch, &s.scratch_bytes, L.total);
   if (rc) return rc;
-  if (!s.status) {
-    MS_CUDA(ctx, cudaMalloc((void**)&s.status, 256));
-    MS_CUDA(ctx, cudaMemset(s.status, 0, 256));
-  }
-  if (s.counters_cap < B) {
-    if (s.counters) cudaFree(s.counters);
-    s.counters = nullptr;
-    s.counters_cap = 0;
-    const int64_t cap = B + B / 8 + 64;
-    MS_CUDA(ctx, cudaMalloc((void**)&s.counters, (size_t)cap * 4));
-    MS_CUDA(ctx, cudaMemset(s.counters, 0, (size_t)cap * 4));
-    s.counters_cap = cap;
-  }
+  rc = ensure_state(ctx, s, B);
+  if (rc) return rc;
   char* base = (char*)s.scratch;
   ms::Args A;
   memset(&A, 0, sizeof A);
@@ -310,10 +366,15 @@ static int run_device(ms_ctx* ctx, DevState& s, const float* logits, int64_t B, 
   A.cands = (ms::Cand*)(base + L.cands);
   A.penbits = (P.use_pen && P.mode != ms::kGreedy) ? (uint32_t*)(base + L.penbits) : nullptr;
   A.status = s.status;
+  A.epoch = next_epoch(s);
+  A.test_wait = ctx->inject_wait;
+  ctx->inject_wait = 0;
   A.row_count = s.counters;
   A.ksum = ms::kKSum;
   A.out_ids = out_ids;
   if (diag) {
+    A.d_pen = diag->pen_logits;
+    A.pen_ld = diag->pen_ld;
     A.cand_cap = diag->cand_cap;
     A.d_cand_ids = diag->cand_cap > 0 ? diag->cand_ids : nullptr;
     A.d_cand_probs = diag->cand_cap > 0 ? diag->cand_probs : nullptr;
@@ -355,6 +416,7 @@ extern "C" int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V,
   const bool host = (flags & MS_HOST_PTRS) != 0, dev = (flags & MS_DEVICE_PTRS) != 0;
   if (host == dev) return fail(ctx, MS_ERR_ARG, "ms_sample: pass exactly one of MS_HOST_PTRS / MS_DEVICE_PTRS");
   if (diag && diag->cand_cap < 0) return fail(ctx, MS_ERR_ARG, "ms_sample: diag->cand_cap < 0");
+  if (diag && diag->pen_logits && diag->pen_ld < V) return fail(ctx, MS_ERR_ARG, "ms_sample: diag->pen_ld < V");
   const ms_params pp = *params;
   const bool greedy = !pp.do_sample || pp.temperature <= 0.0001;
   if (!greedy && !u) return fail(ctx, MS_ERR_ARG, "ms_sample: sampled rows need u[B]");
@@ -371,15 +433,7 @@ extern "C" int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V,
     if (rc == MS_OK && (flags & MS_SYNC)) {
       cudaError_t e = cudaStreamSynchronize(st);
       if (e != cudaSuccess) rc = fail(ctx, MS_ERR_CUDA, "ms_sample: %s", cudaGetErrorString(e));
-      if (rc == MS_OK) {
-        int32_t status = 0;
-        e = cudaMemcpy(&status, s.status, sizeof status, cudaMemcpyDeviceToHost);
-        if (e != cudaSuccess) rc = fail(ctx, MS_ERR_CUDA, "ms_sample: %s", cudaGetErrorString(e));
-        else if (status & ms::kStatusTimeout) {
-          cudaMemset(s.status, 0, sizeof(int32_t));
-          rc = fail(ctx, MS_ERR_TIMEOUT, "ms_sample: a kernel wait timed out");
-        }
-      }
+      if (rc == MS_OK) rc = read_status(ctx, s, "ms_sample");
     }
     cudaSetDevice(prev);
     return rc;
@@ -394,7 +448,7 @@ extern "C" int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V,
   const int nd = (flags & MS_ROW_SHARDED) ? (int)ctx->devs.size() : 1;
   const int64_t per = (B + nd - 1) / nd;
   int rc = MS_OK;
-  struct Slice { int64_t r0, rows; size_t o_logits, o_hist, o_off, o_u, o_out, o_cid, o_cp, o_nc, o_mx, o_sum, o_tot, o_fl; };
+  struct Slice { int64_t r0, rows; size_t o_logits, o_hist, o_off, o_u, o_out, o_cid, o_cp, o_nc, o_mx, o_sum, o_tot, o_fl, o_pen; };
   std::vector<Slice> slices(nd);
   for (int d = 0; d < nd && rc == MS_OK; d++) {
     DevState& s = ctx->devs[d];
@@ -421,6 +475,7 @@ extern "C" int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V,
     sl.o_sum = take((size_t)sl.rows * 8);
     sl.o_tot = take((size_t)sl.rows * 8);
     sl.o_fl = take((size_t)sl.rows * 4);
+    sl.o_pen = take(diag && diag->pen_logits ? (size_t)sl.rows * V * 4 : 4);
     rc = ensure(ctx, &s.io, &s.io_bytes, off);
     if (rc) break;
     char* io = (char*)s.io;
@@ -435,10 +490,13 @@ extern "C" int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V,
     const int32_t* dh = nullptr;
     const int64_t* doff = nullptr;
     if (e == cudaSuccess && hist_off) {
-      std::vector<int64_t> offs((size_t)sl.rows + 1);
+      // rebased offsets, staged in the device state so the host buffer lives
+      // until the stream sync below
+      std::vector<int64_t>& offs = s.host_offs;
+      offs.resize((size_t)sl.rows + 1);
       for (int64_t r = 0; r <= sl.rows; r++) offs[r] = hist_off[sl.r0 + r] - h0;
       if (nh > 0) e = H2D(sl.o_hist, hist + h0, (size_t)nh * 4);
-      if (e == cudaSuccess) e = cudaMemcpy(io + sl.o_off, offs.data(), offs.size() * 8, cudaMemcpyHostToDevice);
+      if (e == cudaSuccess) e = H2D(sl.o_off, offs.data(), offs.size() * 8);
       dh = (const int32_t*)(io + sl.o_hist);
       doff = (const int64_t*)(io + sl.o_off);
     }
@@ -455,6 +513,8 @@ extern "C" int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V,
       dd.row_sum = diag->row_sum ? (double*)(io + sl.o_sum) : nullptr;
       dd.total = diag->total ? (double*)(io + sl.o_tot) : nullptr;
       dd.row_flags = diag->row_flags ? (int32_t*)(io + sl.o_fl) : nullptr;
+      dd.pen_logits = diag->pen_logits ? (float*)(io + sl.o_pen) : nullptr;
+      dd.pen_ld = V;
       dp = &dd;
     }
     rc = run_device(ctx, s, (const float*)(io + sl.o_logits), sl.rows, V, V, dh, doff, &pp,
@@ -475,6 +535,9 @@ extern "C" int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V,
       if (e == cudaSuccess && diag->row_sum) e = D2H(diag->row_sum + sl.r0, sl.o_sum, (size_t)sl.rows * 8);
       if (e == cudaSuccess && diag->total) e = D2H(diag->total + sl.r0, sl.o_tot, (size_t)sl.rows * 8);
       if (e == cudaSuccess && diag->row_flags) e = D2H(diag->row_flags + sl.r0, sl.o_fl, (size_t)sl.rows * 4);
+      if (e == cudaSuccess && diag->pen_logits)
+        e = cudaMemcpy2DAsync(diag->pen_logits + sl.r0 * diag->pen_ld, (size_t)diag->pen_ld * 4, io + sl.o_pen,
+                              (size_t)V * 4, (size_t)V * 4, (size_t)sl.rows, cudaMemcpyDeviceToHost, st);
     }
     if (e != cudaSuccess) { rc = fail(ctx, MS_ERR_CUDA, "ms_sample: D2H: %s", cudaGetErrorString(e)); break; }
   }
@@ -485,15 +548,7 @@ extern "C" int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V,
     cudaSetDevice(s.device);
     cudaError_t e = cudaStreamSynchronize(s.stream);
     if (e != cudaSuccess && rc == MS_OK) rc = fail(ctx, MS_ERR_CUDA, "ms_sample: %s", cudaGetErrorString(e));
-    if (rc == MS_OK) {
-      int32_t status = 0;
-      e = cudaMemcpy(&status, s.status, sizeof status, cudaMemcpyDeviceToHost);
-      if (e != cudaSuccess) rc = fail(ctx, MS_ERR_CUDA, "ms_sample: %s", cudaGetErrorString(e));
-      else if (status & ms::kStatusTimeout) {
-        cudaMemset(s.status, 0, sizeof(int32_t));
-        rc = fail(ctx, MS_ERR_TIMEOUT, "ms_sample: a kernel wait timed out");
-      }
-    }
+    if (rc == MS_OK) rc = read_status(ctx, s, "ms_sample");
   }
   cudaSetDevice(prev);
   return rc;
@@ -573,6 +628,7 @@ extern "C" int ms_sample_noalloc(const float* logits, int64_t B, int64_t V, int6
   A.cands = (ms::Cand*)(scratch + L.cands);
   A.penbits = (P.use_pen && P.mode != ms::kGreedy) ? (uint32_t*)(scratch + L.penbits) : nullptr;
   A.status = (int32_t*)(base + cnt_bytes);
+  A.epoch = 1;  // the status word was cleared above: 1 marks a wait of this call that ran out
   A.row_count = (int32_t*)base;
   A.ksum = ms::kKSum;
   A.out_ids = out_ids;
@@ -622,19 +678,8 @@ extern "C" int ms_shard_records(ms_ctx* ctx, const float* logits, int64_t B, int
   const ScratchLayout L = scratch_layout(B, cols, P);
   int rc = ensure(ctx, &s.scratch, &s.scratch_bytes, L.total + (size_t)B * 4 + 256);
   if (rc) return rc;
-  if (!s.status) {
-    MS_CUDA(ctx, cudaMalloc((void**)&s.status, 256));
-    MS_CUDA(ctx, cudaMemset(s.status, 0, 256));
-  }
-  if (s.counters_cap < B) {
-    if (s.counters) cudaFree(s.counters);
-    s.counters = nullptr;
-    s.counters_cap = 0;
-    const int64_t cap = B + B / 8 + 64;
-    MS_CUDA(ctx, cudaMalloc((void**)&s.counters, (size_t)cap * 4));
-    MS_CUDA(ctx, cudaMemset(s.counters, 0, (size_t)cap * 4));
-    s.counters_cap = cap;
-  }
+  rc = ensure_state(ctx, s, B);
+  if (rc) return rc;
   char* base = (char*)s.scratch;
   ms::Args A = param_args(P, params);
   A.logits = logits;
@@ -647,6 +692,7 @@ extern "C" int ms_shard_records(ms_ctx* ctx, const float* logits, int64_t B, int
   A.stats = (ms::ChunkStat*)(base + L.stats);
   A.cands = (ms::Cand*)(base + L.cands);
   A.status = s.status;
+  A.epoch = next_epoch(s);
   A.row_count = s.counters;
   A.out_ids = (int32_t*)(base + align_up(L.total, 256));  // greedy chunk kernel's per-shard ids (unused)
   A.rec = (unsigned char*)records;

@@ -8,9 +8,8 @@
 //   softmax term fp32(exp(double(x') - double(mx)))            (:14)
 //   probability  fp32(double(e) / sum)                         (:15)
 // CUDA's double `/` and `*` are IEEE round-to-nearest; __double2float_rn is the
-// fp32 store.  `exp` is CUDA's double exp (<= 1 ulp), so the fp32 term can
-// differ from V8's only when the double result sits next to an fp32 rounding
-// midpoint.
+// fp32 store.  The exact softmax term uses js_exp below, the published fdlibm
+// exp method that V8's Math.exp ports, so it equals V8's term bit for bit.
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -33,8 +32,10 @@ constexpr int kRecHead = 32;             // vocab-shard record: header bytes
 constexpr int kRecCand = 16;             // bytes per listed candidate
 constexpr int kTieSlack = 32;            // list room beyond top_k for ties at a shard's k-th value
 
-// Status bits written by kernels (host maps them to MS_ERR_*).
-constexpr int kStatusTimeout = 0x1;
+// The device status word.  A kernel whose bounded wait runs out stores the
+// call's epoch there (Args::epoch, never 0); the host and the later kernels of
+// the same call compare it with that epoch, so a timeout never leaks into a
+// later call and the word needs no clearing between calls.
 
 struct ChunkStat {
   float m;        // max of the penalised logits of the chunk (NaN ignored; -inf if none)
@@ -79,7 +80,12 @@ struct Args {
   Cand* cands;           // [B, n_chunks, kCap]
   uint32_t* penbits;     // [B, ceil(V/32)] penalty bitmap (slow path), may be null
   int32_t* out_ids;      // [B]
-  int32_t* status;       // device status word
+  int32_t* status;       // device status word (see above)
+  int32_t epoch;         // this call's epoch (> 0)
+  long long test_wait;   // > 0: the first chunk CTA waits this many cycles on an
+                         // mbarrier nothing completes (ms_debug_inject)
+  float* d_pen;          // diagnostics: penalised logits [B, pen_ld] (may be null)
+  int64_t pen_ld;
   // vocabulary shards (0 / null otherwise)
   int32_t col0;          // global column of local column 0 (penalty ids are global)
   int32_t G;             // merge: shards per row
@@ -140,8 +146,69 @@ __device__ __forceinline__ float temper_fast(float x, double T, double rT, int t
   return temper ? div_to_f32((double)x, T, rT) : x;
 }
 
+// Math.exp as V8 computes it: fdlibm's exp (e_exp.c), which V8 ports in
+// src/base/ieee754.cc.  x = k*ln2 + r with |r| <= ln2/2 and ln2 split so that
+// k*ln2_hi is exact; on that range r*(e^r + 1)/(e^r - 1) ~ 2 + P1 z + ... + P5 z^5
+// (z = r^2, fdlibm's Remez coefficients), so e^r = 1 + r + r*c/(2 - c) with
+// c = r - z*(P1 + ...), and e^x = 2^k e^r.  Every step is one IEEE double
+// operation in fdlibm's order (explicit _rn intrinsics: nothing is contracted
+// into an FMA).
+static __device__ __noinline__ double js_exp(double x) {
+  const double ln2_hi = 6.93147180369123816490e-01, ln2_lo = 1.90821492927058770002e-10;
+  const double inv_ln2 = 1.44269504088896338700e+00;
+  const double p1 = 1.66666666666666019037e-01, p2 = -2.77777777770155933842e-03,
+               p3 = 6.61375632143793436117e-05, p4 = -1.65339022054652515390e-06,
+               p5 = 4.13813679705723846039e-08;
+  const long long bx = __double_as_longlong(x);
+  const uint32_t hw = (uint32_t)((unsigned long long)bx >> 32);
+  const int neg = (int)(hw >> 31);
+  const uint32_t ahw = hw & 0x7fffffffu;
+  if (ahw >= 0x40862E42u) {  // |x| >= 709.78, or not finite
+    if (ahw >= 0x7ff00000u) {
+      if (((ahw & 0xfffffu) | (uint32_t)bx) != 0u) return __dadd_rn(x, x);  // NaN
+      return neg ? 0.0 : x;
+    }
+    if (x > 7.09782712893383973096e+02) return __longlong_as_double(0x7ff0000000000000ll);
+    if (x < -7.45133219101941108420e+02) return 0.0;
+  }
+  double hi = 0.0, lo = 0.0, r;
+  int k = 0;
+  if (ahw > 0x3FD62E42u) {    // |x| > ln2/2
+    if (ahw < 0x3FF0A2B2u) {  // |x| < 1.5 ln2: k = +-1
+      if (x == 1.0) return 2.718281828459045;  // V8 returns E here
+      hi = neg ? __dadd_rn(x, ln2_hi) : __dsub_rn(x, ln2_hi);
+      lo = neg ? -ln2_lo : ln2_lo;
+      k = neg ? -1 : 1;
+    } else {
+      k = __double2int_rz(__dadd_rn(__dmul_rn(inv_ln2, x), neg ? -0.5 : 0.5));
+      const double t = (double)k;
+      hi = __dsub_rn(x, __dmul_rn(t, ln2_hi));  // exact
+      lo = __dmul_rn(t, ln2_lo);
+    }
+    r = __dsub_rn(hi, lo);
+  } else if (ahw < 0x3e300000u) {  // |x| < 2^-28
+    return __dadd_rn(1.0, x);
+  } else {
+    r = x;
+  }
+  const double z = __dmul_rn(r, r);
+  double q = __dadd_rn(p4, __dmul_rn(z, p5));
+  q = __dadd_rn(p3, __dmul_rn(z, q));
+  q = __dadd_rn(p2, __dmul_rn(z, q));
+  q = __dadd_rn(p1, __dmul_rn(z, q));
+  const double c = __dsub_rn(r, __dmul_rn(z, q));
+  if (k == 0) return __dsub_rn(1.0, __dsub_rn(__ddiv_rn(__dmul_rn(r, c), __dsub_rn(c, 2.0)), r));
+  const double y = __dsub_rn(1.0, __dsub_rn(__dsub_rn(lo, __ddiv_rn(__dmul_rn(r, c), __dsub_rn(2.0, c))), hi));
+  if (k >= -1021) {
+    if (k == 1024) return __dmul_rn(__dmul_rn(y, 2.0), __longlong_as_double(0x7fe0000000000000ll));
+    return __dmul_rn(y, __longlong_as_double((long long)(0x3ff + k) << 52));  // exact
+  }
+  return __dmul_rn(__dmul_rn(y, __longlong_as_double((long long)(0x3ff + k + 1000) << 52)),
+                   __longlong_as_double(0x0170000000000000ll));  // * 2^-1000
+}
+
 __device__ __forceinline__ float term_exact(float xp, float mxp) {
-  return __double2float_rn(exp((double)xp - (double)mxp));
+  return __double2float_rn(js_exp(__dsub_rn((double)xp, (double)mxp)));
 }
 
 __device__ __forceinline__ float prob_exact(float e, double S) {

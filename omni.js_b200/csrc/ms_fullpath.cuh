@@ -556,6 +556,64 @@ __device__ FullSel select_full(const RowInfo& R, FullSmem& sm, bool by_mass, dou
   return out;
 }
 
+// Diagnostics of a whole-row selection: the first c = min(n, cand_cap, kExtCap)
+// candidates in (prob desc, id asc) order with their exact probabilities.  The
+// element at rank c fixes the last key kc; every candidate has x >= the low end
+// of kc's probability tie group, and exactly c elements have a key <= kc.
+__device__ void full_emit_cands(const Args& A, int r, const RowInfo& R, FullSmem& sm, long long n) {
+  const int c = (int)min((long long)min(A.cand_cap, kExtCap), n);
+  if (c <= 0 || !(A.d_cand_ids || A.d_cand_probs)) return;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const FullSel s = select_full(R, sm, false, (double)c);
+  __shared__ float e_xlo;
+  __shared__ unsigned long long e_kc;
+  if (warp == 0) {
+    const float xc = load_x(R, s.id);
+    const float xlo = tie_low(R, xc);
+    if ((tid & 31) == 0) {
+      e_xlo = xlo;
+      e_kc = ((unsigned long long)(0xFFFFFFFFu - __float_as_uint(prob_of(R, xc))) << 32) | (uint32_t)s.id;
+      sm.n_ext = 0;
+    }
+  }
+  __syncthreads();
+  const float xlo = e_xlo;
+  const unsigned long long kc = e_kc;
+  for_row(R, [&](float x, int i) {
+    if (!(x >= xlo)) return;
+    const unsigned long long k =
+        ((unsigned long long)(0xFFFFFFFFu - __float_as_uint(prob_of(R, x))) << 32) | (uint32_t)i;
+    if (k > kc) return;
+    const int pos = atomicAdd(&sm.n_ext, 1);
+    if (pos < kExtCap) sm.key[pos] = k;
+  });
+  __syncthreads();
+  const int m = min(sm.n_ext, kExtCap);  // == c
+  int np2 = 1;
+  while (np2 < m) np2 <<= 1;
+  for (int j = m + tid; j < np2; j += (int)blockDim.x) sm.key[j] = ~0ull;
+  __syncthreads();
+  for (int kk = 2; kk <= np2; kk <<= 1) {
+    for (int jj = kk >> 1; jj > 0; jj >>= 1) {
+      for (int i = tid; i < np2; i += (int)blockDim.x) {
+        const int ixj = i ^ jj;
+        if (ixj > i) {
+          const unsigned long long x = sm.key[i], y = sm.key[ixj];
+          if ((x > y) == ((i & kk) == 0)) { sm.key[i] = y; sm.key[ixj] = x; }
+        }
+      }
+      __syncthreads();
+    }
+  }
+  for (int i = tid; i < m; i += (int)blockDim.x) {
+    const unsigned long long k = sm.key[i];
+    if (A.d_cand_ids) A.d_cand_ids[(int64_t)r * A.cand_cap + i] = (int32_t)(uint32_t)k;
+    if (A.d_cand_probs)
+      A.d_cand_probs[(int64_t)r * A.cand_cap + i] = __uint_as_float(0xFFFFFFFFu - (uint32_t)(k >> 32));
+  }
+  __syncthreads();
+}
+
 // Top-k / top-p / draw for one row over the whole vocabulary (src/generation.js:27-49).
 __device__ __forceinline__ void full_path(const Args& A, int r, const RowInfo& R, FullSmem& sm, int flags) {
   const int tid = threadIdx.x;
@@ -606,5 +664,6 @@ __device__ __forceinline__ void full_path(const Args& A, int r, const RowInfo& R
     if (A.d_total) A.d_total[r] = total;
     if (A.d_row_flags) A.d_row_flags[r] = flags | MS_ROW_FULLVOCAB;
   }
+  full_emit_cands(A, r, R, sm, n);
 }
 }  // namespace ms

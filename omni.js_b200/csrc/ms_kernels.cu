@@ -526,6 +526,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
   extern __shared__ __align__(128) unsigned char dyn_smem[];
   float* tile = reinterpret_cast<float*>(dyn_smem);
   __shared__ __align__(8) uint64_t bar[kSub];
+  __shared__ __align__(8) uint64_t stall_bar;  // test hook: an mbarrier nothing completes
   __shared__ uint32_t penmask[kChunk / 32];
   __shared__ int is_last;
   __shared__ int q_cnt;  // candidates found (may exceed kCap: overflow)
@@ -540,12 +541,13 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
   const int n = min(kChunk, A.V - c0);
   const float* g = A.logits + (int64_t)r * A.ld + c0;
   const bool bulk = ((reinterpret_cast<uintptr_t>(g) & 15) == 0) && ((n & 3) == 0);
+  const bool stall = A.test_wait > 0 && r == 0 && c == 0;
 
   if (tid == 0) {
-    if (bulk) {
+    if (bulk)
       for (int s = 0; s < kSub; s++) mbar_init(&bar[s], 1);
-      fence_mbar_init();
-    }
+    if (stall) mbar_init(&stall_bar, 1);
+    if (bulk || stall) fence_mbar_init();
   }
   if (PEN) penmask[tid] = 0u;  // kChunk / 32 == kThreads words
   if (tid == 0) q_cnt = 0;
@@ -590,11 +592,14 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     for (int s = 0; s < kSub; s++)
       if (s * kSubElems < n && !mbar_wait(&bar[s], 0, kWaitCycles)) timed_out = 1;
   }
+  // test hook (ms_debug_inject): no arrival ever completes stall_bar's phase, so
+  // this wait runs out after A.test_wait cycles; no copy is issued against it
+  if (stall && tid == 0 && !mbar_wait(&stall_bar, 0, A.test_wait)) timed_out = 1;
   if (__syncthreads_or(timed_out)) {
-    // The call fails (status word); the CTA still runs to the end on whatever
-    // the tile holds, so the row counters stay consistent.
+    // The call fails (status word = this call's epoch); the CTA still runs to
+    // the end on whatever the tile holds, so the row counters stay consistent.
     if (tid == 0) {
-      atomicOr(A.status, kStatusTimeout);
+      atomicExch(A.status, A.epoch);
       if (bulk)  // let any copy still in flight land before going on (bounded)
         for (int s = 0; s < kSub; s++)
           if (s * kSubElems < n) mbar_wait(&bar[s], 0, kWaitCycles);
@@ -612,6 +617,12 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
       tile[j] = pen_apply_fast(tile[j], A.pen, A.rpen);
     }
     __syncthreads();
+  }
+  // diagnostics: the penalised logits, the reference's `work` before the
+  // temperature divide (src/generation.js:72-75)
+  if (A.d_pen) {
+    float* dp = A.d_pen + (int64_t)r * A.pen_ld + c0;
+    for (int j = tid; j < n; j += kThreads) dp[j] = tile[j];
   }
 
   const float4* t4 = reinterpret_cast<const float4*>(tile);
@@ -787,8 +798,12 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
   __syncthreads();
   if (is_last) {
     __threadfence();
-    if (!(*((volatile int32_t*)A.status) & kStatusTimeout))
+    if (*((volatile int32_t*)A.status) != A.epoch) {
       finalize_row<kGreedy>(A, r, *reinterpret_cast<FinSmem*>(dyn_smem));
+    } else if (tid == 0) {  // a wait of this call ran out: the row has no id
+      A.out_ids[r] = -1;
+      if (A.d_row_flags) A.d_row_flags[r] = MS_ROW_TIMEOUT;
+    }
   }
 }
 
@@ -800,7 +815,13 @@ template <int MODE, int NT>
 __global__ void __launch_bounds__(NT, kThreads * 2 / NT) finalize_kernel(const __grid_constant__ Args A) {
   extern __shared__ __align__(128) unsigned char fin_smem[];
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  if (*((volatile int32_t*)A.status) & kStatusTimeout) return;
+  if (*((volatile int32_t*)A.status) == A.epoch) {  // a wait of this call ran out
+    if (threadIdx.x == 0) {
+      A.out_ids[blockIdx.x] = -1;
+      if (A.d_row_flags) A.d_row_flags[blockIdx.x] = MS_ROW_TIMEOUT;
+    }
+    return;
+  }
   finalize_row<MODE>(A, blockIdx.x, *reinterpret_cast<FinSmem*>(fin_smem));
 }
 
@@ -921,7 +942,7 @@ __global__ void __launch_bounds__(256, 4) shard_kernel(const __grid_constant__ A
     }
     return;
   }
-  const int timed_out = *((volatile int32_t*)A.status) & kStatusTimeout;
+  const int timed_out = *((volatile int32_t*)A.status) == A.epoch;
   row_stats(A, r, F);
   if (F.nan_row || timed_out) {
     if (tid == 0) {
@@ -1202,6 +1223,18 @@ cudaError_t launch_merge(const Args& A, cudaStream_t stream) {
   if (e != cudaSuccess) return e;
   if (A.mode == kGreedy) merge_kernel<kGreedy><<<dim3(A.B), dim3(256), kShardSmem, stream>>>(A);
   else merge_kernel<kTopK><<<dim3(A.B), dim3(256), kShardSmem, stream>>>(A);
+  return cudaGetLastError();
+}
+
+__global__ void exp_kernel(const double* x, double* y, int64_t n) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = js_exp(x[i]);
+}
+
+// The exact-term exp over n doubles (test hook: checked against the oracle's).
+cudaError_t launch_exp(const double* x, double* y, int64_t n, cudaStream_t stream) {
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 8);
+  exp_kernel<<<(unsigned)blocks, 256, 0, stream>>>(x, y, n);
   return cudaGetLastError();
 }
 

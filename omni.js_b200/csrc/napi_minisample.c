@@ -5,7 +5,7 @@
  *          history: Int32Array | null, historyOffsets: Int32Array | null,
  *          opts: {doSample, temperature, topK, topP, repetitionPenalty},
  *          uniforms: Float64Array | null) -> Int32Array(B)
- *   status() -> {abi: number, devices: number}
+ *   status() -> {abi: number}   (the library's MS_ABI_VERSION)
  *
  * `opts` is the object normalizeOptions returns (src/generation.js:57-68).
  * The call is synchronous, like generateTokens (src/generation.js:97-114).
@@ -94,7 +94,19 @@ static napi_value js_sample(napi_env env, napi_callback_info info) {
       napi_throw_type_error(env, NULL, "minisample.sample: historyOffsets must have B+1 entries");
       return NULL;
     }
+    /* offsets must index inside `history`: off[0] >= 0, ascending, off[B] <= its length */
+    int ok = off32[0] >= 0 && (int64_t)off32[B] <= (int64_t)nh;
+    for (int64_t i = 0; ok && i < B; i++) ok = off32[i + 1] >= off32[i];
+    if (!ok) {
+      napi_throw_range_error(env, NULL,
+                             "minisample.sample: historyOffsets must ascend from >= 0 to <= history.length");
+      return NULL;
+    }
     off = (int64_t*)malloc(sizeof(int64_t) * (size_t)(B + 1));
+    if (!off) {
+      napi_throw_error(env, NULL, "minisample: out of host memory");
+      return NULL;
+    }
     for (int64_t i = 0; i <= B; i++) off[i] = off32[i];
   }
   ms_params p;

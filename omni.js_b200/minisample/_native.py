@@ -33,6 +33,11 @@ MS_ROW_NAN = 0x2
 MS_ROW_FULLVOCAB = 0x4
 MS_ROW_SLOWPATH = 0x8
 MS_ROW_UNSETTLED = 0x10
+MS_ROW_TIMEOUT = 0x20
+
+MS_INJECT_WAIT = 1
+MS_INJECT_ALLOC = 2
+ABI_VERSION = 2
 
 ERROR_NAMES = {
     MS_ERR_ARG: "MS_ERR_ARG", MS_ERR_CUDA: "MS_ERR_CUDA", MS_ERR_NCCL: "MS_ERR_NCCL",
@@ -43,7 +48,7 @@ ERROR_NAMES = {
 # Every symbol include/minisample.h declares.
 EXPORTED = ("ms_version", "ms_create", "ms_destroy", "ms_last_error", "ms_sample", "ms_profile_read",
             "ms_scratch_bytes", "ms_sample_noalloc", "ms_launch_count", "ms_shard_record_bytes",
-            "ms_shard_records", "ms_merge_records")
+            "ms_shard_records", "ms_merge_records", "ms_debug_inject", "ms_debug_exp")
 
 
 class MsParams(ctypes.Structure):
@@ -66,6 +71,8 @@ class MsDiag(ctypes.Structure):
         ("row_sum", ctypes.c_void_p),
         ("total", ctypes.c_void_p),
         ("row_flags", ctypes.c_void_p),
+        ("pen_logits", ctypes.c_void_p),
+        ("pen_ld", ctypes.c_int64),
     ]
 
 
@@ -124,6 +131,10 @@ def load(path: str | None = None):
     L.ms_scratch_bytes.restype = ctypes.c_int
     L.ms_scratch_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.POINTER(MsParams),
                                    ctypes.POINTER(ctypes.c_int64)]
+    L.ms_debug_exp.restype = ctypes.c_int
+    L.ms_debug_exp.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
+    L.ms_debug_inject.restype = ctypes.c_int
+    L.ms_debug_inject.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int64]
     L.ms_sample_noalloc.restype = ctypes.c_int
     L.ms_sample_noalloc.argtypes = [
         ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p,

@@ -98,6 +98,11 @@ class Sampler:
         self._check(self._L.ms_profile_read(self._ctx, ctypes.byref(a), ctypes.byref(b), ctypes.byref(n)))
         return a.value, b.value, n.value
 
+    def inject(self, what: int, arg: int) -> None:
+        """Failure injection for the next call (ms_debug_inject): N.MS_INJECT_WAIT
+        with a cycle count, or N.MS_INJECT_ALLOC."""
+        self._check(self._L.ms_debug_inject(self._ctx, int(what), int(arg)))
+
     def launch_count(self) -> int:
         """Kernels this context has launched since it was created."""
         n = ctypes.c_int64()
@@ -125,7 +130,7 @@ class Sampler:
         if ua is not None and ua.shape[0] < B:
             raise ValueError("u must have B entries")
         ids = out if out is not None else np.empty(B, np.int32)
-        D, keep = self._host_diag(B, diag, cand_cap)
+        D, keep = self._host_diag(B, V, diag, cand_cap)
         p = params.to_c()
         flags = N.MS_HOST_PTRS | (N.MS_ROW_SHARDED if row_sharded else 0) | (N.MS_PROFILE if profile else 0)
         rc = self._L.ms_sample(self._ctx, x.ctypes.data, B, V, ld,
@@ -139,7 +144,9 @@ class Sampler:
         return ids
 
     @staticmethod
-    def _host_diag(B, diag, cand_cap):
+    def _host_diag(B, V, diag, cand_cap):
+        """diag: False, True (row diagnostics), or "pen" (also the penalised
+        logits [B, V])."""
         if not diag:
             return None, None
         keep = {
@@ -148,6 +155,10 @@ class Sampler:
             "row_flags": np.zeros(B, np.int32),
         }
         D = N.MsDiag()
+        if diag == "pen":
+            keep["pen_logits"] = np.zeros((B, V), np.float32)
+            D.pen_logits = keep["pen_logits"].ctypes.data
+            D.pen_ld = V
         D.cand_cap = int(cand_cap)
         if cand_cap > 0:
             keep["cand_ids"] = np.full((B, cand_cap), -1, np.int32)
@@ -184,6 +195,10 @@ class Sampler:
                 "row_flags": torch.zeros(B, dtype=torch.int32, device=dev),
             }
             D = N.MsDiag()
+            if diag == "pen":
+                keep["pen_logits"] = torch.zeros((B, V), dtype=torch.float32, device=dev)
+                D.pen_logits = keep["pen_logits"].data_ptr()
+                D.pen_ld = V
             D.cand_cap = int(cand_cap)
             if cand_cap > 0:
                 keep["cand_ids"] = torch.full((B, cand_cap), -1, dtype=torch.int32, device=dev)

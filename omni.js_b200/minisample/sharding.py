@@ -83,12 +83,19 @@ def gather_rows(shard_rows, group=None):
 
 
 def sample_vocab_sharded(sampler, logits_shard, col0: int, V: int, params, u, hist=None, hist_off=None,
-                         group=None):
+                         group=None, resolve: bool = True):
     """Vocabulary-sharded sampling, one rank per column shard: the shard's
     records, an all-to-all so each rank merges a block of rows, an all-gather
-    of the ids.  Rows the shard lists cannot settle (-1, rare ties) are sampled
-    from their gathered whole rows.  u: [B] fp64 CUDA uniforms (every rank the
-    same).  Returns the [B] int32 ids on every rank."""
+    of the ids.  u: [B] fp64 CUDA uniforms (every rank the same).  Returns the
+    [B] int32 ids on every rank.
+
+    Rows the shard lists cannot settle (rare probability ties at a shard's
+    cut) come back as -1.  With resolve=True they are then sampled from their
+    gathered whole rows; that needs the ids on the host (one small copy, the
+    same on every rank, so every rank takes the same collective steps).  With
+    resolve=False nothing waits on the host: the caller gets the -1 rows and
+    resolves them later with resolve_unsettled (bench loops keep the device
+    busy this way)."""
     import torch
     import torch.distributed as dist
 
@@ -103,17 +110,29 @@ def sample_vocab_sharded(sampler, logits_shard, col0: int, V: int, params, u, hi
         sampler.merge_records(recs[: r1 - r0], V, params, u=u[r0:r1], out=blk[: r1 - r0])
     allb = torch.empty((world * Bb,), dtype=torch.int32, device=logits_shard.device)
     dist.all_gather_into_tensor(allb, blk, group=group)
-    ids = allb[:B].clone()
-    bad = torch.nonzero(ids < 0).flatten()
-    n_bad = torch.tensor([bad.numel()], device=ids.device)
-    dist.all_reduce(n_bad, op=dist.ReduceOp.MAX, group=group)  # same collectives on every rank
-    if int(n_bad.item()) > 0:
-        rows = gather_rows(logits_shard[bad], group)
-        sub_h = sub_o = None
-        if hist_off is not None:
-            offs = hist_off.cpu().numpy()
-            hs = [hist[int(offs[i]):int(offs[i + 1])] for i in bad.tolist()]
-            sub_h = torch.cat(hs) if hs else hist[:0]
-            sub_o = torch.tensor([0] + [int(x.numel()) for x in hs], dtype=torch.int64).cumsum(0).to(ids.device)
-        ids[bad] = sampler.sample(rows.contiguous(), params, u=u[bad].contiguous(), hist=sub_h, hist_off=sub_o)
+    ids = allb[:B]
+    if resolve:
+        ids = resolve_unsettled(sampler, ids, logits_shard, params, u, hist, hist_off, group)
+    return ids
+
+
+def resolve_unsettled(sampler, ids, logits_shard, params, u, hist=None, hist_off=None, group=None):
+    """Samples the rows whose id is -1 from their whole rows (gathered from the
+    column shards).  Every rank holds the same ids, so every rank finds the same
+    rows and runs the same collectives."""
+    import torch
+
+    bad = torch.nonzero(ids.cpu() < 0).flatten().tolist()
+    if not bad:
+        return ids
+    ids = ids.clone()
+    bad_d = torch.tensor(bad, dtype=torch.int64, device=ids.device)
+    rows = gather_rows(logits_shard[bad_d], group)
+    sub_h = sub_o = None
+    if hist_off is not None:
+        offs = hist_off.cpu().numpy()
+        hs = [hist[int(offs[i]):int(offs[i + 1])] for i in bad]
+        sub_h = torch.cat(hs) if hs else hist[:0]
+        sub_o = torch.tensor([0] + [int(x.numel()) for x in hs], dtype=torch.int64).cumsum(0).to(ids.device)
+    ids[bad_d] = sampler.sample(rows.contiguous(), params, u=u[bad_d].contiguous(), hist=sub_h, hist_off=sub_o)
     return ids

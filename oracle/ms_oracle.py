@@ -4,9 +4,12 @@ ctypes wrapper of oracle/ms_oracle.c, the C restatement of mini.js's sampler
 (src/generation.js:9-81).  Only tests/, __graft_entry__.smoke() and bench.py's
 CPU-baseline leg import this module.
 
-Parity status: unpinned (no JavaScript engine here; the reference's tests pin
-no sampled value).  tests/golden/ holds known-answer cases derived by hand from
-the JS source.
+Math.exp is V8's (a restatement of fdlibm's exp, the method V8 ports); the C
+library's exp can be selected with set_exp(libc=True) for comparisons.
+Parity is pinned to the reference's arithmetic, not to a run of the reference
+(no JavaScript engine exists on these machines; the reference's tests pin no
+sampled value): tests/golden/ holds known-answer cases derived by hand from the
+JS source, and an independent restatement of fdlibm's exp checks the oracle's.
 """
 from __future__ import annotations
 
@@ -80,12 +83,38 @@ def lib():
         L.msref_sample_batch.argtypes = [
             ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
             ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(Params), ctypes.c_void_p,
-            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+            ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
         ]
+        L.msref_set_exp.restype = None
+        L.msref_set_exp.argtypes = [ctypes.c_int]
+        L.msref_exp.restype = ctypes.c_double
+        L.msref_exp.argtypes = [ctypes.c_double]
+        L.msref_terms_both.restype = None
+        L.msref_terms_both.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_double, ctypes.c_void_p,
+                                       ctypes.c_void_p]
         L.msref_row_diag_size.restype = ctypes.c_int
         assert L.msref_row_diag_size() == ctypes.sizeof(RowDiag), "RowDiag layout mismatch"
         _lib = L
     return _lib
+
+
+def set_exp(libc: bool = False) -> None:
+    """Math.exp as V8 computes it (default), or the C library's exp."""
+    lib().msref_set_exp(1 if libc else 0)
+
+
+def js_exp(x: float) -> float:
+    """The oracle's Math.exp (whichever set_exp selected)."""
+    return lib().msref_exp(float(x))
+
+
+def terms_both(xs, mx: float):
+    """fp32(exp(x - mx)) for every x with V8's exp and with the C library's."""
+    xs = np.ascontiguousarray(xs, dtype=np.float32)
+    a = np.empty(xs.shape[0], np.float32)
+    b = np.empty(xs.shape[0], np.float32)
+    lib().msref_terms_both(xs.ctypes.data, xs.shape[0], float(mx), a.ctypes.data, b.ctypes.data)
+    return a, b
 
 
 def make_params(do_sample=True, temperature=1.0, top_k=50, top_p=0.95, repetition_penalty=1.0):
@@ -139,8 +168,10 @@ def _diag_dict(d: RowDiag) -> dict:
 
 
 def sample_batch(logits, hist=None, hist_off=None, params=None, u=None, nthreads=None,
-                 cand_cap=0, want_diag=True):
-    """B independent pickToken calls.  Returns (ids[B], diag dict of arrays or None)."""
+                 cand_cap=0, want_diag=True, want_pen=False):
+    """B independent pickToken calls.  Returns (ids[B], diag dict of arrays or None);
+    with want_pen the diag also holds "pen_logits" [B, V], each row's `work`
+    after the repetition penalty (src/generation.js:72-75)."""
     logits = np.ascontiguousarray(logits, dtype=np.float32)
     B, V = logits.shape
     p = params if params is not None else make_params()
@@ -161,10 +192,11 @@ def sample_batch(logits, hist=None, hist_off=None, params=None, u=None, nthreads
             diags[r].cand_probs = cps[r].ctypes.data_as(ctypes.POINTER(ctypes.c_float))
     if nthreads is None:
         nthreads = os.cpu_count() or 1
+    pen = np.empty((B, V), np.float32) if want_pen else None
     rc = lib().msref_sample_batch(logits.ctypes.data, B, V, V, _ptr(hist_a), _ptr(off_a),
                                   ctypes.byref(p), _ptr(u_a), out.ctypes.data,
                                   ctypes.cast(diags, ctypes.c_void_p) if diags is not None else None,
-                                  int(nthreads))
+                                  int(nthreads), _ptr(pen))
     if rc != 0:
         raise RuntimeError("oracle batch failed")
     if not want_diag:
@@ -175,4 +207,6 @@ def sample_batch(logits, hist=None, hist_off=None, params=None, u=None, nthreads
     if cand_cap > 0:
         dd["cand_ids"] = cids
         dd["cand_probs"] = cps
+    if want_pen:
+        dd["pen_logits"] = pen
     return out, dd

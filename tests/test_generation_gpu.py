@@ -133,15 +133,16 @@ def test_generate_async_equals_sync(oracle):
 
 
 @pytest.mark.parametrize("case", [0, 1, 2])
-def test_generate_tokens_batch_matches_per_row(case):
-    """Row i of the batched loop equals generate_tokens on row i with the same
-    uniform stream; a row that hits EOS or onToken=false stops alone."""
-    from minisample.generation import generate_tokens, generate_tokens_batch, set_backend
+def test_generate_tokens_batch_matches_oracle_loop(oracle, case):
+    """Row i of the batched loop equals the oracle's generation loop on row i
+    with the same uniform stream; a row that hits EOS or onToken=false stops
+    alone."""
+    from minisample.generation import generate_tokens_batch, set_backend
 
     set_backend("cuda")
     opts = dict(CASES[case])
     inputs = [[1, 2, 3], [7], [4, 4, 4, 4], [9, 8]]
-    per_row = [generate_tokens(StubModel(40 + i), inputs[i], opts, rand=_mulberry(60 + i)[0])
+    per_row = [_oracle_loop(oracle, StubModel(40 + i), inputs[i], opts, _mulberry(60 + i)[0])
                for i in range(len(inputs))]
     eos = per_row[1][2]  # makes row 1 stop at its third id (and any other row that draws it)
     stop_at = {3: 2}     # row 3 stops after its second id

@@ -27,7 +27,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     assert set(decl) == set(_native.EXPORTED), decl
     for name in decl:
         assert hasattr(L, name), name
-    assert L.ms_version() == 1
+    assert L.ms_version() == _native.ABI_VERSION
     out = subprocess.run(["nm", "-D", "--defined-only", _native.LIB_PATH], capture_output=True, text=True,
                          check=True).stdout
     for name in decl:
@@ -114,3 +114,38 @@ def test_workload_generators_shapes_and_determinism():
     assert 100 < rep < 330  # about 10% of 2048 positions repeat an earlier id
     z = W.logits_np(W.WORKLOADS["qwen2_b256"], 1, B=64)
     assert (z.max(axis=1) > 9).sum() > 10  # peaked rows exist
+
+
+def test_argument_checks_that_need_no_gpu():
+    """Size and pointer checks that run before any CUDA call: the allocation-free
+    entry point, the scratch sizing, the shard record sizing and the test
+    hooks."""
+    from minisample import SampleParams
+    from minisample import _native as N
+
+    L = N.load()
+    p = SampleParams(True, 0.9, 64, 0.9, 1.2).to_c()
+    g = SampleParams(False).to_c()
+    dummy = ctypes.c_void_p(16)  # never dereferenced: every call below is rejected first
+    call = L.ms_sample_noalloc
+    assert call(dummy, 4, 0, 1, None, None, ctypes.byref(p), dummy, dummy, None) == N.MS_ERR_ARG      # V < 1
+    assert call(dummy, 4, 100, 99, None, None, ctypes.byref(p), dummy, dummy, None) == N.MS_ERR_ARG   # ld < V
+    assert call(dummy, -1, 100, 100, None, None, ctypes.byref(p), dummy, dummy, None) == N.MS_ERR_ARG
+    assert call(dummy, 4, 2**31, 2**31, None, None, ctypes.byref(p), dummy, dummy, None) == N.MS_ERR_ARG
+    assert call(None, 4, 100, 100, None, None, ctypes.byref(p), dummy, dummy, None) == N.MS_ERR_ARG
+    assert call(dummy, 4, 100, 100, None, dummy, ctypes.byref(p), dummy, dummy, None) == N.MS_ERR_ARG  # off w/o hist
+    assert call(dummy, 4, 100, 100, None, None, ctypes.byref(p), None, dummy, None) == N.MS_ERR_ARG    # needs u
+    assert call(dummy, 4, 100, 100, None, None, None, dummy, dummy, None) == N.MS_ERR_ARG
+    assert call(dummy, 0, 100, 100, None, None, ctypes.byref(g), None, dummy, None) == N.MS_OK         # B = 0
+    # 512 x 262144 with top-k needs ~50 MiB of scratch: beyond the fixed array
+    assert call(dummy, 512, 262144, 262144, None, None, ctypes.byref(p), dummy, dummy, None) == N.MS_ERR_SCRATCH
+    out = ctypes.c_int64()
+    assert L.ms_scratch_bytes(-1, 100, ctypes.byref(p), ctypes.byref(out)) == N.MS_ERR_ARG
+    assert L.ms_scratch_bytes(4, 0, ctypes.byref(p), ctypes.byref(out)) == N.MS_ERR_ARG
+    assert L.ms_scratch_bytes(4, 100, None, ctypes.byref(out)) == N.MS_ERR_ARG
+    assert L.ms_shard_record_bytes(0, ctypes.byref(p), ctypes.byref(out)) == N.MS_ERR_ARG
+    assert L.ms_debug_inject(None, N.MS_INJECT_WAIT, 10) == N.MS_ERR_ARG
+    assert L.ms_debug_exp(None, None, -1, None) == N.MS_ERR_ARG
+    assert L.ms_debug_exp(None, None, 0, None) == N.MS_OK
+    for fn in (L.ms_destroy, L.ms_launch_count):
+        assert (fn(None) if fn is L.ms_destroy else fn(None, ctypes.byref(out))) == N.MS_ERR_ARG

@@ -2,7 +2,8 @@
 seeded inputs.
 
 Tolerances (the sampler's contract):
-  * penalised/tempered max and candidate ids / order: bit-exact;
+  * penalised logits (the reference's `work` after the penalty), the
+    tempered max and the candidate ids / order: bit-exact;
   * probabilities: within 1e-5 relative;
   * sampled ids: identical, except rows whose draw r, or whose running top-p
     sum, lies within 1e-6 of a cumulative-probability boundary in the oracle;
@@ -10,6 +11,7 @@ Tolerances (the sampler's contract):
 """
 import json
 import os
+import time
 
 import numpy as np
 import pytest
@@ -26,44 +28,62 @@ def params(oracle, sp):
     return oracle.make_params(sp.do_sample, sp.temperature, sp.top_k, sp.top_p, sp.repetition_penalty)
 
 
-def run_both(oracle, sampler, X, sp, u=None, hist=None, off=None, cap=64):
-    from minisample import SampleParams  # noqa: F401
-
-    ids_r, d_r = oracle.sample_batch(X, hist, off, params(oracle, sp), u, cand_cap=cap)
-    ids_g, d_g = sampler.sample(X, sp, u=u, hist=hist, hist_off=off, diag=True, cand_cap=cap)
+def run_both(oracle, sampler, X, sp, u=None, hist=None, off=None, cap=64, pen=True):
+    ids_r, d_r = oracle.sample_batch(X, hist, off, params(oracle, sp), u, cand_cap=cap, want_pen=pen)
+    ids_g, d_g = sampler.sample(X, sp, u=u, hist=hist, hist_off=off, diag="pen" if pen else True, cand_cap=cap)
     return ids_r, d_r, ids_g, d_g
 
 
 def check(ids_r, d_r, ids_g, d_g, sp, label="", cap=64, max_boundary_frac=0.02):
+    """Compare one batch; returns the rows whose id differs within the
+    boundary tolerance.  A row near a boundary still has its candidate list
+    compared up to the shorter of the two cuts."""
     B = len(ids_r)
     tolerated = []
     greedy = (not sp.do_sample) or sp.temperature <= 1e-4
     for r in range(B):
-        near = (d_r["margin_draw"][r] < BOUNDARY) or (d_r["margin_cut"][r] < BOUNDARY)
+        near_draw = d_r["margin_draw"][r] < BOUNDARY
+        near_cut = d_r["margin_cut"][r] < BOUNDARY
+        near = near_draw or near_cut
         if ids_r[r] != ids_g[r]:
             assert near and not greedy, (
                 f"{label} row {r}: gpu {ids_g[r]} oracle {ids_r[r]} "
                 f"margins draw={d_r['margin_draw'][r]:.3g} cut={d_r['margin_cut'][r]:.3g} "
                 f"flags={d_g['row_flags'][r]}")
             tolerated.append(r)
-            continue
         if greedy or d_r["nan_path"][r]:
             continue
         # tempered max is an fp32 value in both
         assert d_g["row_max"][r] == d_r["mx"][r], (label, r)
         assert abs(d_g["row_sum"][r] - d_r["sum"][r]) <= 1e-6 * d_r["sum"][r], (label, r)
-        if near:
-            continue
-        assert d_g["n_cand"][r] == d_r["n_cand"][r], (label, r, d_g["n_cand"][r], d_r["n_cand"][r])
-        assert abs(d_g["total"][r] - d_r["total"][r]) <= 1e-6 * max(d_r["total"][r], 1e-30), (label, r)
-        if "cand_ids" in d_g and not (d_g["row_flags"][r] & 0x4):
-            n = min(int(d_r["n_cand"][r]), cap)
+        n = int(d_r["n_cand"][r])
+        if not near_cut:
+            assert d_g["n_cand"][r] == n, (label, r, d_g["n_cand"][r], n)
+            assert abs(d_g["total"][r] - d_r["total"][r]) <= 1e-6 * max(d_r["total"][r], 1e-30), (label, r)
+        if "cand_ids" in d_g:
+            n = min(n, int(d_g["n_cand"][r]), cap)
             np.testing.assert_array_equal(d_g["cand_ids"][r, :n], d_r["cand_ids"][r, :n], err_msg=f"{label} r{r}")
             np.testing.assert_allclose(d_g["cand_probs"][r, :n], d_r["cand_probs"][r, :n], rtol=PROB_RTOL,
                                        err_msg=f"{label} r{r}")
+    if "pen_logits" in d_g and "pen_logits" in d_r:
+        ga, ra = np.ascontiguousarray(d_g["pen_logits"]), np.ascontiguousarray(d_r["pen_logits"])
+        diff = (ga.view(np.uint32) != ra.view(np.uint32)) & ~(np.isnan(ga) & np.isnan(ra))
+        bad = np.argwhere(diff)
+        assert bad.shape[0] == 0, f"{label}: {bad.shape[0]} penalised logits differ, first {bad[:3].tolist()}"
     frac = len(tolerated) / max(B, 1)
     assert frac <= max_boundary_frac, f"{label}: {len(tolerated)}/{B} boundary rows"
     return tolerated
+
+
+def report(name, **kv):
+    """Parity figures of a full-size case: printed, and appended as a JSON line
+    to $MS_PARITY_REPORT when that is set."""
+    line = dict(case=name, **kv)
+    print(json.dumps(line))
+    path = os.environ.get("MS_PARITY_REPORT")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps(line) + "\n")
 
 
 # ------------------------------------------------------------------ known answers
@@ -195,13 +215,23 @@ def _workload(name, B, seed=11):
     return w, X, hist, off, u
 
 
-@pytest.mark.parametrize("name,B", [("llama3_b64_greedy", 16), ("llama3_b64", 24), ("qwen2_b256", 8),
-                                    ("gemma_b512", 24), ("vocab_sharded", 8)])
-def test_workload_parity(oracle, sampler, name, B):
-    w, X, hist, off, u = _workload(name, B)
+@pytest.mark.parametrize("name", ["llama3_b64_greedy", "llama3_b64", "qwen2_b256", "gemma_b512", "vocab_sharded"])
+def test_workload_parity_full_batch(oracle, sampler, name):
+    """Every row of the workload's full batch against the oracle: ids,
+    penalised logits (bit-exact), row max and sum, candidate lists (for
+    whole-vocabulary rows too), n_cand and total; the boundary rows are
+    reported."""
+    from minisample import workloads as W
+
+    w = W.WORKLOADS[name]
+    w_, X, hist, off, u = _workload(name, w.B, seed=5)
+    t0 = time.time()
     ids_r, d_r, ids_g, d_g = run_both(oracle, sampler, X, w.params, u, hist, off)
     tol = check(ids_r, d_r, ids_g, d_g, w.params, name)
-    print(f"{name}: {B} rows, {len(tol)} boundary rows")
+    flags = d_g["row_flags"]
+    report(name, rows=int(w.B), vocab=int(w.V), boundary_rows=len(tol), boundary_frac=len(tol) / w.B,
+           id_mismatch=int(np.sum(ids_r != ids_g)), fullvocab_rows=int(np.sum((flags & 0x4) != 0)),
+           slowpath_rows=int(np.sum((flags & 0x8) != 0)), seconds=round(time.time() - t0, 1))
 
 
 @pytest.mark.parametrize("name,B", [("gpt2_b1", 16), ("llama3_b64", 16), ("gemma_b512", 16)])
@@ -259,15 +289,13 @@ def test_gpt2_b1_generation_loop(oracle, sampler):
     assert tolerated <= 2
 
 
-def test_full_size_gemma_b512(oracle, sampler):
-    """The full 512 x 262144 batch: every id checked against the oracle."""
+def test_gemma_b512_rows_mostly_on_candidate_path(oracle, sampler):
+    """The headline workload's rows are settled from the chunk candidates: at
+    most a handful take the exact rescan."""
     w, X, hist, off, u = _workload("gemma_b512", 512, seed=5)
-    ids_g, d_g = sampler.sample(X, w.params, u=u, hist=hist, hist_off=off, diag=True, cand_cap=64)
-    ids_r, d_r = oracle.sample_batch(X, hist, off, params(oracle, w.params), u, cand_cap=64)
-    check(ids_r, d_r, ids_g, d_g, w.params, "gemma_b512 full")
+    ids_g, d_g = sampler.sample(X, w.params, u=u, hist=hist, hist_off=off, diag=True)
     slow = int(np.sum((d_g["row_flags"] & 0x8) != 0))
-    print(f"gemma_b512 full: slow-path rows {slow}/512")
-    assert slow <= 8
+    assert slow <= 8, slow
 
 
 def test_repeatable(sampler):
