@@ -325,3 +325,34 @@ def test_default_stream_ordering(sampler):
         sampler.sample(x, w.params, u=u, hist=hd, hist_off=od, out=out, sync=False)
         got = out.clone()  # queued right behind the sampler's kernels
         assert torch.equal(got, ref)
+
+
+@pytest.mark.parametrize("pen", [0.5, 0.8, 1.2, 3.0])
+@pytest.mark.parametrize("H", [40, 2500, 5000])
+def test_penalty_edge_histories(oracle, sampler, pen, H):
+    """The repetition penalty on top-k calls: rows where it lowers the maximum
+    (pen > 1), raises low values above the candidates (pen < 1), hits every top
+    candidate, or repeats ids; short and long histories, including ids outside
+    the vocabulary."""
+    from minisample import SampleParams
+
+    rng = np.random.default_rng(int(pen * 100) + H)
+    B, V = 6, 70000
+    X = rng.normal(0.0, 2.0, (B, V)).astype(np.float32)
+    X[3] = np.float32(-5.0)  # a row of equal values with a few peaks
+    X[3, rng.choice(V, 50, replace=False)] = np.float32(4.0)
+    rows = []
+    for r in range(B):
+        h = rng.integers(-2, V + 2, H)
+        if r == 1:  # the row's largest logits are all in the history
+            h[: min(H, 300)] = np.argsort(-X[r])[: min(H, 300)]
+        if r == 2:  # low values that a penalty < 1 lifts toward the top
+            h[: min(H, 200)] = np.argsort(X[r])[: min(H, 200)]
+        h[::7] = h[0]  # repeats count once
+        rows.append(h.astype(np.int32))
+    hist = np.concatenate(rows)
+    off = np.arange(0, (B + 1) * H, H, dtype=np.int64)
+    u = rng.random(B)
+    for sp in (SampleParams(True, 0.9, 64, 0.9, pen), SampleParams(True, 1.3, 8, 1.0, pen)):
+        ids_r, d_r, ids_g, d_g = run_both(oracle, sampler, X, sp, u, hist, off)
+        check(ids_r, d_r, ids_g, d_g, sp, f"pen {pen} H {H} k {sp.top_k}", max_boundary_frac=0.34)
