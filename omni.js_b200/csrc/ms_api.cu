@@ -103,6 +103,8 @@ ms::Args param_args(const Plan& P, const ms_params* p) {
 
 struct ScratchLayout {
   size_t stats = 0, cands = 0, penbits = 0, total = 0;
+  // whole-vocabulary rows: chunk histograms, plans, extraction lists
+  size_t h_cnt = 0, h_mass = 0, plan = 0, lists = 0, list_cnt = 0;
 };
 
 ScratchLayout scratch_layout(int64_t B, int64_t V, const Plan& P) {
@@ -114,6 +116,18 @@ ScratchLayout scratch_layout(int64_t B, int64_t V, const Plan& P) {
   if (P.mode != ms::kGreedy) off = align_up(off + (size_t)B * P.n_chunks * ms::kCap * sizeof(ms::Cand), 256);
   L.penbits = off;
   if (P.use_pen && P.mode != ms::kGreedy) off = align_up(off + (size_t)B * ((V + 31) / 32) * 4, 256);
+  if (P.mode == ms::kFull) {
+    L.h_cnt = off;
+    off = align_up(off + (size_t)B * P.n_chunks * ms::kNB * sizeof(uint16_t), 256);
+    L.h_mass = off;
+    off = align_up(off + (size_t)B * P.n_chunks * ms::kNB * sizeof(double), 256);
+    L.plan = off;
+    off = align_up(off + (size_t)B * sizeof(ms::NucPlan), 256);
+    L.lists = off;
+    off = align_up(off + (size_t)B * 2 * ms::kListCap * sizeof(ms::Cand), 256);
+    L.list_cnt = off;
+    off = align_up(off + (size_t)B * 4 * sizeof(int32_t), 256);
+  }
   L.total = off;
   return L;
 }
@@ -365,6 +379,14 @@ static int run_device(ms_ctx* ctx, DevState& s, const float* logits, int64_t B, 
   A.stats = (ms::ChunkStat*)(base + L.stats);
   A.cands = (ms::Cand*)(base + L.cands);
   A.penbits = (P.use_pen && P.mode != ms::kGreedy) ? (uint32_t*)(base + L.penbits) : nullptr;
+  if (P.mode == ms::kFull) {
+    // counts only for rank selection (top_k above the candidate path)
+    A.h_cnt = (P.k > 0 && P.k < V) ? (uint16_t*)(base + L.h_cnt) : nullptr;
+    A.h_mass = (double*)(base + L.h_mass);
+    A.plan = (ms::NucPlan*)(base + L.plan);
+    A.lists = (ms::Cand*)(base + L.lists);
+    A.list_cnt = (int32_t*)(base + L.list_cnt);
+  }
   A.status = s.status;
   A.epoch = next_epoch(s);
   A.test_wait = ctx->inject_wait;
@@ -627,6 +649,14 @@ extern "C" int ms_sample_noalloc(const float* logits, int64_t B, int64_t V, int6
   A.stats = (ms::ChunkStat*)(scratch + L.stats);
   A.cands = (ms::Cand*)(scratch + L.cands);
   A.penbits = (P.use_pen && P.mode != ms::kGreedy) ? (uint32_t*)(scratch + L.penbits) : nullptr;
+  if (P.mode == ms::kFull) {
+    // counts only for rank selection (top_k above the candidate path)
+    A.h_cnt = (P.k > 0 && P.k < V) ? (uint16_t*)(scratch + L.h_cnt) : nullptr;
+    A.h_mass = (double*)(scratch + L.h_mass);
+    A.plan = (ms::NucPlan*)(scratch + L.plan);
+    A.lists = (ms::Cand*)(scratch + L.lists);
+    A.list_cnt = (int32_t*)(scratch + L.list_cnt);
+  }
   A.status = (int32_t*)(base + cnt_bytes);
   A.epoch = 1;  // the status word was cleared above: 1 marks a wait of this call that ran out
   A.row_count = (int32_t*)base;

@@ -28,6 +28,13 @@ constexpr int kGathMax = 4096;          // candidates >= the row threshold the f
 constexpr int kFinMax = 1024;           // candidates the finalizer ranks exactly
 constexpr int kKSum = 64;               // candidates kept for the sum correction when top_k is off
 
+// Whole-vocabulary rows (top_k off or above kKmax): mass histograms.  A bin is
+// 1/16 of a log2 unit of the tempered logit: bin(x) = floor(-x * 16 * log2(e) / T),
+// one grid for every chunk of every row; a chunk's histogram covers kNB bins
+// from its own top bin down (the last one also holds everything below).
+constexpr int kNB = 512;
+constexpr int kListCap = 8192;          // elements of one extraction range a row can hold
+
 constexpr int kRecHead = 32;             // vocab-shard record: header bytes
 constexpr int kRecCand = 16;             // bytes per listed candidate
 constexpr int kTieSlack = 32;            // list room beyond top_k for ties at a shard's k-th value
@@ -51,6 +58,26 @@ struct Cand {
   float x;        // penalised (untempered) logit
   int32_t i;      // vocabulary id
 };
+
+// Selection plan of one whole-vocabulary row (nucleus_plan_kernel): the row's
+// mass histogram located the top-p cut and the draw in one or two bin ranges,
+// whose elements nucleus_extract_kernel copies out and nucleus_resolve_kernel
+// ranks exactly.
+struct NucPlan {
+  int32_t flags;         // kPlanDone: outputs already written; kPlanFallback: exact whole-row path
+  int32_t b_row;         // absolute histogram bin of the row max (row bin 0)
+  int32_t nr;            // extraction ranges (0, 1 or 2)
+  int32_t cut_rg;        // range holding the cut (-1: no cut, every element is a candidate)
+  int32_t draw_rg;       // range holding the draw
+  int32_t lo[2], hi[2];  // the ranges, in row bins (inclusive)
+  int32_t pad;
+  int64_t cnt_above[2];  // elements in the row bins above each range
+  double mass_above[2];  // their fast probability mass
+  double mass_tot;       // fast probability mass of the row
+  double S;              // softmax denominator
+  float M, Mp;           // penalised max, tempered max
+};
+constexpr int kPlanDone = 1, kPlanFallback = 2;
 
 enum Mode : int32_t { kGreedy = 0, kTopK = 1, kFull = 2 };
 
@@ -80,6 +107,12 @@ struct Args {
   Cand* cands;           // [B, n_chunks, kCap]
   uint32_t* penbits;     // [B, ceil(V/32)] penalty bitmap (slow path), may be null
   int32_t* out_ids;      // [B]
+  // whole-vocabulary rows (mode kFull)
+  uint16_t* h_cnt;       // [B, n_chunks, kNB] elements per chunk bin
+  double* h_mass;        // [B, n_chunks, kNB] their fast masses, in units of the chunk's zref term
+  struct NucPlan* plan;  // [B] the row's selection plan (nucleus_plan_kernel)
+  Cand* lists;           // [B, 2, kListCap] elements of the plan's extraction ranges
+  int32_t* list_cnt;     // [B, 4]: elements in each range, elements above each range
   int32_t* status;       // device status word (see above)
   int32_t epoch;         // this call's epoch (> 0)
   long long test_wait;   // > 0: the first chunk CTA waits this many cycles on an

@@ -520,6 +520,17 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   full_path(A, r, R, *reinterpret_cast<FullSmem*>(&F), flags);
 }
 
+// Absolute mass-histogram bin of a logit: floor(-x * a16) with a16 = 16 * a
+// (1/16 of a log2 unit of the tempered logit per bin), saturating; the same
+// arithmetic wherever a bin is computed, so every pass agrees on it.
+__device__ __forceinline__ int nuc_bin(float x, float a16) { return __float2int_rd(__fmul_rn(-x, a16)); }
+// Per-bin fixed-point scale of the chunk histogram's masses (see sample_kernel).
+__device__ __forceinline__ float nuc_scale(int b) { return ex2_approx(21.f + (float)b * 0.0625f); }
+__device__ __forceinline__ int nuc_local(int bin, int top) {
+  const long long d = (long long)bin - (long long)top;
+  return (int)(d < 0 ? 0 : (d > kNB - 1 ? kNB - 1 : d));
+}
+
 // =============================================================== the kernel
 template <int MODE, bool PEN>
 __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_constant__ Args A) {
@@ -551,6 +562,23 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
   }
   if (PEN) penmask[tid] = 0u;  // kChunk / 32 == kThreads words
   if (tid == 0) q_cnt = 0;
+  // whole-vocabulary rows: the chunk's mass histogram.  Counts (packed u16
+  // pairs) only when a rank is selected (top_k above kKmax).  Masses in one
+  // 32-bit word per bin, scaled per bin: an element of local bin b has a fast
+  // term e within 2^(+-1/16) of 2^(-b/16), so q = e * hscale[b] with
+  // hscale[b] = 2^(21 + b/16) is below 2^21.1, rounded to within 2^-22 of
+  // its value (one atomic per element, no carry word).  A bin of more than
+  // about 1900 elements can wrap the word: the chunk then marks its histogram
+  // invalid (mass NaN) and the row takes the exact whole-row path.
+  uint32_t* hcnt = reinterpret_cast<uint32_t*>(dyn_smem + kChunk * sizeof(float));
+  uint32_t* hq = hcnt + kNB / 2;
+  float* hscale = reinterpret_cast<float*>(hq + kNB);
+  __shared__ int hwrap;
+  if (tid == 0) hwrap = 0;
+  if constexpr (MODE == kFull) {
+    for (int b = tid; b < kNB / 2 + kNB; b += kThreads) hcnt[b] = 0u;
+    for (int b = tid; b < kNB; b += kThreads) hscale[b] = nuc_scale(b);
+  }
   __syncthreads();
   if (bulk) {
     if (tid == 0) {
@@ -710,6 +738,17 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     const float zref = zok ? zr : __int_as_float(0x7fc00000);
     float s = 0.f, comp = 0.f;
     uint32_t cmask = 0;  // bit i: this thread's float4 of step i holds an element >= sig
+    const float a16 = __fmul_rn(a, 16.f);
+    const int btop = nuc_bin(m, a16);  // the chunk's top bin (INT_MAX: a chunk of -inf)
+    const bool hcounts = A.h_cnt != nullptr;
+    auto hist_add = [&](float x, float e) {
+      if (x != x) return;  // a NaN makes the whole row NaN
+      const int lb = nuc_local(nuc_bin(x, a16), btop);
+      if (hcounts) atomicAdd(&hcnt[lb >> 1], 1u << ((lb & 1) << 4));
+      const uint32_t q = __float2uint_rn(__fmul_rn(e, hscale[lb]));
+      const uint32_t old = atomicAdd(&hq[lb], q);
+      if (old + q < old) hwrap = 1;
+    };
     auto kahan = [&](float t) {
       const float y = __fsub_rn(t, comp);
       const float ss = __fadd_rn(s, y);
@@ -729,6 +768,13 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
         const float2 t2 = f2_unpack(f2_add(e01, e23));
         kahan(__fadd_rn(t2.x, t2.y));
         cmask |= (uint32_t)(fmaxf(fmax3(v.x, v.y, v.z), v.w) >= sig) << i;
+        if constexpr (MODE == kFull) {
+          const float2 ea = f2_unpack(e01), eb = f2_unpack(e23);
+          hist_add(v.x, ea.x);
+          hist_add(v.y, ea.y);
+          hist_add(v.z, eb.x);
+          hist_add(v.w, eb.y);
+        }
       }
     } else {
       // partial chunk, or zref out of range: one element at a time
@@ -742,6 +788,8 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
         for (int l = 0; l < 4; l++) {
           e[l] = zok ? term_fast_z(xs[l], a, zref) : term_fast(xs[l], mref, a);
           if (j + l >= n) e[l] = 0.f;  // padding past the row end contributes nothing
+          if constexpr (MODE == kFull)
+            if (j + l < n) hist_add(xs[l], e[l]);
         }
         kahan(__fadd_rn(__fadd_rn(e[0], e[2]), __fadd_rn(e[1], e[3])));
         cmask |= (uint32_t)(fmaxf(fmax3(v.x, v.y, v.z), v.w) >= sig) << i;
@@ -774,8 +822,17 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
       if (lane == 0) {
         ChunkStat st;
         st.m = m; st.tau = tau; st.s = S; st.n_cand = min(q_cnt, kCap + 1);
-        st.best_i = INT_MAX; st.zref = zref; st.sig = sig;
+        // whole-vocabulary rows keep the chunk's top histogram bin here
+        st.best_i = (MODE == kFull) ? btop : INT_MAX;
+        st.zref = zref; st.sig = sig;
         A.stats[(int64_t)r * A.n_chunks + c] = st;
+      }
+    }
+    if constexpr (MODE == kFull) {
+      const int64_t hb = ((int64_t)r * A.n_chunks + c) * kNB;
+      for (int b = tid; b < kNB; b += kThreads) {
+        if (hcounts) A.h_cnt[hb + b] = (uint16_t)((hcnt[b >> 1] >> ((b & 1) << 4)) & 0xFFFFu);
+        A.h_mass[hb + b] = hwrap ? __longlong_as_double(0x7ff8000000000000ll) : (double)hq[b] / (double)hscale[b];
       }
     }
   }
@@ -1116,6 +1173,12 @@ __global__ void __launch_bounds__(256, 4) merge_kernel(const __grid_constant__ A
   }
 }
 
+}  // namespace ms
+
+#include "ms_nucleus.cuh"
+
+namespace ms {
+
 static_assert(sizeof(FinSmem) <= kChunk * sizeof(float), "finalize scratch must fit in the chunk tile");
 static_assert(sizeof(FullSmem) <= kChunk * sizeof(float), "full-row scratch must fit in the chunk tile");
 static_assert(kChunk / 32 == kThreads, "one penalty bitmap word per thread");
@@ -1123,11 +1186,43 @@ static_assert(kChunk / 32 == kThreads, "one penalty bitmap word per thread");
 // =============================================================== launch
 namespace {
 constexpr size_t kSmem = (size_t)kChunk * sizeof(float);
+// whole-vocabulary chunk kernels also hold the chunk's mass histogram
+constexpr size_t kSmemFull = kSmem + (size_t)(kNB / 2 + 2 * kNB) * sizeof(uint32_t);  // counts, masses, scales
+constexpr size_t kResSmem = sizeof(ResSmem) > sizeof(FullSmem) ? sizeof(ResSmem) : sizeof(FullSmem);
+
+template <int MODE>
+constexpr size_t chunk_smem() { return MODE == kFull ? kSmemFull : kSmem; }
 
 template <int MODE, bool PEN>
 cudaError_t set_attrs() {
   return cudaFuncSetAttribute((const void*)sample_kernel<MODE, PEN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              (int)kSmem);
+                              (int)chunk_smem<MODE>());
+}
+
+cudaError_t set_nuc_attrs() {
+  cudaError_t e = cudaFuncSetAttribute((const void*)nucleus_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sizeof(NucSmem));
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute((const void*)nucleus_resolve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kResSmem);
+  return e;
+}
+
+// A launch that may start while the grid before it on the stream finishes
+// (it waits with griddepcontrol.wait where it needs that grid's results).
+template <typename K>
+cudaError_t launch_pdl(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, const Args& S) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, S);
 }
 
 constexpr size_t kFinSmem = sizeof(FullSmem) > sizeof(FinSmem) ? sizeof(FullSmem) : sizeof(FinSmem);
@@ -1140,11 +1235,18 @@ cudaError_t set_fin_attrs() {
 
 template <int MODE, bool PEN>
 cudaError_t launch_mode(const Args& S, dim3 grid, cudaStream_t stream, cudaEvent_t mid) {
-  sample_kernel<MODE, PEN><<<grid, dim3(kThreads), kSmem, stream>>>(S);
+  sample_kernel<MODE, PEN><<<grid, dim3(kThreads), chunk_smem<MODE>(), stream>>>(S);
   cudaError_t e = cudaGetLastError();
   if (mid) cudaEventRecord(mid, stream);
   if constexpr (MODE == kGreedy) {
     return e;  // the chunk kernel's last CTA of each row picks its id
+  } else if constexpr (MODE == kFull) {
+    // whole-vocabulary rows: plan, extract, resolve
+    if (e == cudaSuccess) e = launch_pdl(nucleus_plan_kernel, dim3(S.B), dim3(kNB), sizeof(NucSmem), stream, S);
+    if (e == cudaSuccess)
+      e = launch_pdl(nucleus_extract_kernel<PEN>, dim3(S.B, S.n_chunks), dim3(256), 0, stream, S);
+    if (e == cudaSuccess) e = launch_pdl(nucleus_resolve_kernel, dim3(S.B), dim3(kNB), kResSmem, stream, S);
+    return e;
   } else {
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
@@ -1253,7 +1355,7 @@ cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev, i
     if (e == cudaSuccess) e = set_attrs<kFull, true>();
     if (e == cudaSuccess) e = set_fin_attrs<kTopK, 256>();
     if (e == cudaSuccess) e = set_fin_attrs<kTopK, kThreads>();
-    if (e == cudaSuccess) e = set_fin_attrs<kFull, kThreads>();
+    if (e == cudaSuccess) e = set_nuc_attrs();
     if (e != cudaSuccess) return e;
     attrs_done[dev] = true;
   }
@@ -1270,6 +1372,13 @@ cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev, i
     S.row_count = A.row_count + r0;
     S.cands = A.cands + r0 * A.n_chunks * kCap;
     if (A.penbits) S.penbits = A.penbits + r0 * ((A.V + 31) / 32);
+    if (A.h_cnt) {
+      S.h_cnt = A.h_cnt + r0 * A.n_chunks * kNB;
+      S.h_mass = A.h_mass + r0 * A.n_chunks * kNB;
+      S.plan = A.plan + r0;
+      S.lists = A.lists + r0 * 2 * kListCap;
+      S.list_cnt = A.list_cnt + r0 * 4;
+    }
     S.out_ids = A.out_ids + r0;
     if (A.d_cand_ids) S.d_cand_ids = A.d_cand_ids + r0 * A.cand_cap;
     if (A.d_cand_probs) S.d_cand_probs = A.d_cand_probs + r0 * A.cand_cap;
@@ -1300,7 +1409,7 @@ cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev, i
     }
     if (prof) cudaEventRecord(ev[2], stream);
     if (e != cudaSuccess) return e;
-    if (launched) *launched += (A.mode == kGreedy) ? 1 : 2;
+    if (launched) *launched += (A.mode == kGreedy) ? 1 : (A.mode == kFull ? 4 : 2);
   }
   return cudaSuccess;
 }
