@@ -39,6 +39,7 @@ struct RowInfo {
   float nat16;         // fp32(16 / T): level-0 buckets per logit unit
   double T;
   int temper;
+  double rT, rS;       // fp64(1 / T), fp64(1 / S): divides by multiplication (exact-divide fallback)
 };
 
 struct Hist {
@@ -72,8 +73,11 @@ __device__ __forceinline__ float load_x(const RowInfo& R, int i) {
 __device__ __forceinline__ double mass_fast(const RowInfo& R, float x) {
   return (double)term_fast(x, R.M, R.a) * R.mscale;
 }
+// The reference's probability of logit x: fp32(fp32(exp(fp32(x / T) - mx)) / sum),
+// each divide a multiplication by the reciprocal unless the product sits next
+// to an fp32 rounding midpoint (div_to_f32), so the result is the same.
 __device__ __forceinline__ float prob_of(const RowInfo& R, float x) {
-  return prob_exact(term_exact(temper_exact(x, R.T, R.temper), R.Mp), R.S);
+  return div_to_f32((double)term_exact(temper_fast(x, R.T, R.rT, R.temper), R.Mp), R.S, R.rS);
 }
 __device__ __forceinline__ int bin0(const RowInfo& R, float x) {
   // 1/16-nat buckets below the max; monotone (non-increasing) in x
@@ -126,20 +130,29 @@ __device__ __forceinline__ void for_row(const RowInfo& R, F f) {
 }
 
 // Keys [lo, hi] with pred(lo) true and pred monotone (true, then false as the
-// key grows): returns the largest key with pred true.  One warp evaluates 32
-// probes per round.  `dir` -1 searches downward (pred true at hi, returns the
-// smallest key with pred true).
+// key grows): returns the largest key with pred true.  One warp: a first round
+// probes the offsets 2^0 .. 2^31 from the start (a probability-tie group
+// usually spans few keys), then each round splits what is left 32 ways.  `dir`
+// -1 searches downward (pred true at hi, returns the smallest key with pred true).
 template <typename Pred>
 __device__ uint32_t warp_boundary_search(uint32_t lo, uint32_t hi, int dir, Pred pred) {
   const int lane = threadIdx.x & 31;
   const uint64_t base = dir > 0 ? lo : hi;
   uint64_t L = 0, H = (uint64_t)hi - lo;
+  auto at = [&](uint64_t p) { return dir > 0 ? (uint32_t)(base + p) : (uint32_t)(base - p); };
+  if (H > 0) {  // galloping round
+    const uint64_t p = min((uint64_t)1 << lane, H);
+    const unsigned msk = __ballot_sync(0xffffffffu, pred(at(p)));
+    const int ntrue = __popc(msk);  // pred is monotone: the lanes below the boundary
+    if (ntrue > 0) L = min((uint64_t)1 << (ntrue - 1), H);
+    if (ntrue < 32) H = min((uint64_t)1 << ntrue, H) - 1;
+    if (L > H) H = L;
+  }
   while (H > L) {
     const uint64_t step = (H - L + 31) / 32;
     uint64_t p = L + (uint64_t)(lane + 1) * step;
     if (p > H) p = H;
-    const uint32_t key = dir > 0 ? (uint32_t)(base + p) : (uint32_t)(base - p);
-    const bool t = pred(key);
+    const bool t = pred(at(p));
     const unsigned msk = __ballot_sync(0xffffffffu, t);
     const int ntrue = __popc(msk);
     const uint64_t p_last = __shfl_sync(0xffffffffu, p, ntrue > 0 ? ntrue - 1 : 0);
@@ -152,7 +165,7 @@ __device__ uint32_t warp_boundary_search(uint32_t lo, uint32_t hi, int dir, Pred
       else if (p_last >= H) H = L;
     }
   }
-  return dir > 0 ? (uint32_t)(base + L) : (uint32_t)(base - L);
+  return at(L);
 }
 
 // Smallest / largest x with prob_of(x) == prob_of(v); one full warp.  The

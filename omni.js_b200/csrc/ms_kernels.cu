@@ -481,6 +481,8 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   R.temper = A.temper;
   R.rpen = A.rpen;
   R.nat16 = (float)(16.0 / A.T);
+  R.rT = A.rT;
+  R.rS = 1.0 / R.S;
 
   if (MODE == kTopK && !F.slow) {
     // every element outside the candidates has x < tau_row, so its probability
@@ -1202,6 +1204,8 @@ cudaError_t set_attrs() {
 cudaError_t set_nuc_attrs() {
   cudaError_t e = cudaFuncSetAttribute((const void*)nucleus_plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)sizeof(NucSmem));
+  for (const void* f : {(const void*)nucleus_extract_kernel<false>, (const void*)nucleus_extract_kernel<true>})
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute((const void*)nucleus_resolve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)kResSmem);
@@ -1244,7 +1248,7 @@ cudaError_t launch_mode(const Args& S, dim3 grid, cudaStream_t stream, cudaEvent
     // whole-vocabulary rows: plan, extract, resolve
     if (e == cudaSuccess) e = launch_pdl(nucleus_plan_kernel, dim3(S.B), dim3(kNB), sizeof(NucSmem), stream, S);
     if (e == cudaSuccess)
-      e = launch_pdl(nucleus_extract_kernel<PEN>, dim3(S.B, S.n_chunks), dim3(256), 0, stream, S);
+      e = launch_pdl(nucleus_extract_kernel<PEN>, dim3(S.B, S.n_chunks), dim3(kThreads), kSmem, stream, S);
     if (e == cudaSuccess) e = launch_pdl(nucleus_resolve_kernel, dim3(S.B), dim3(kNB), kResSmem, stream, S);
     return e;
   } else {

@@ -280,11 +280,15 @@ __global__ void __launch_bounds__(kNB, 2) nucleus_plan_kernel(const __grid_const
 // The chunk grid in reverse order (the last chunks streamed are first, while
 // they are still in L2): every element of the chunk whose row bin lies in one
 // of its row's plan ranges goes to that range's list, and the elements above
-// each range are counted.  A bin range [b1, b2] is the float interval
+// each range are counted.  The chunk comes into shared memory by bulk copies,
+// as in sample_kernel.  A bin range [b1, b2] is the float interval
 // b1 <= -x * a16 < b2 + 1 of the same product nuc_bin floors (exact: the bounds
 // are integers below 2^24), so the test is two compares.
 template <bool PEN>
-__global__ void __launch_bounds__(256) nucleus_extract_kernel(const __grid_constant__ Args A) {
+__global__ void __launch_bounds__(kThreads, 3) nucleus_extract_kernel(const __grid_constant__ Args A) {
+  extern __shared__ __align__(128) unsigned char ext_smem[];
+  float* tile = reinterpret_cast<float*>(ext_smem);
+  __shared__ __align__(8) uint64_t bar[kSub];
   __shared__ uint32_t penmask[kChunk / 32];
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");  // the plans
@@ -307,76 +311,118 @@ __global__ void __launch_bounds__(256) nucleus_extract_kernel(const __grid_const
   if ((float)__ldcg(&A.stats[(int64_t)r * A.n_chunks + c].best_i) >= fmaxf(fhi[0], fhi[1])) return;
   const int c0 = c * kChunk;
   const int n = min(kChunk, A.V - c0);
-  if (PEN) {
-    for (int w = tid; w < kChunk / 32; w += blockDim.x) penmask[w] = 0u;
-    __syncthreads();
+  const float* g = A.logits + (int64_t)r * A.ld + c0;
+  const bool bulk = ((reinterpret_cast<uintptr_t>(g) & 15) == 0) && ((n & 3) == 0);
+  if (tid == 0 && bulk) {
+    for (int s = 0; s < kSub; s++) mbar_init(&bar[s], 1);
+    fence_mbar_init();
+  }
+  if (PEN) penmask[tid] = 0u;  // kChunk / 32 == kThreads words
+  __syncthreads();
+  if (bulk) {
+    if (tid == 0)
+      for (int s = 0; s < kSub; s++) {
+        const int b = s * kSubElems, cnt = min(kSubElems, n - b);
+        if (cnt > 0) {
+          mbar_expect_tx(&bar[s], (uint32_t)cnt * 4u);
+          bulk_g2s(tile + b, g + b, (uint32_t)cnt * 4u, &bar[s]);
+        }
+      }
+  } else {
+    for (int j = tid; j < n; j += kThreads) tile[j] = __ldg(g + j);
+  }
+  for (int j = n + tid; j < kChunk; j += kThreads) tile[j] = __int_as_float(0x7fc00000);  // padding fails every test
+  if (PEN) {  // the chunk's penalty bitmap while the copies fly
     const int64_t h0 = A.hist_off[r], h1 = A.hist_off[r + 1];
-    for (int64_t h = h0 + tid; h < h1; h += blockDim.x) {
+    for (int64_t h = h0 + tid; h < h1; h += kThreads) {
       const uint32_t d = (uint32_t)__ldg(A.hist + h) - (uint32_t)c0;  // ids outside wrap past n
       if (d < (uint32_t)n) atomicOr(&penmask[d >> 5], 1u << (d & 31));
     }
-    __syncthreads();
   }
-  const float* g = A.logits + (int64_t)r * A.ld + c0;
-  Cand* out0 = A.lists + (int64_t)(2 * r) * kListCap;
-  Cand* out1 = out0 + kListCap;
-  const bool vec = ((reinterpret_cast<uintptr_t>(g) & 15) == 0);
-  const int step = 4 * (int)blockDim.x;
-  const int rounds = (n + step - 1) / step;  // warp-uniform: every lane runs every round
-  auto load4 = [&](int j0, float* xs) {
-    if (vec && j0 + 3 < n) {
-      const float4 v = __ldg(reinterpret_cast<const float4*>(g + j0));
-      xs[0] = v.x; xs[1] = v.y; xs[2] = v.z; xs[3] = v.w;
-    } else {
-#pragma unroll
-      for (int l = 0; l < 4; l++) xs[l] = j0 + l < n ? __ldg(g + j0 + l) : __int_as_float(0x7fc00000);
+  int timed_out = 0;
+  if (bulk && tid == 0)
+    for (int s = 0; s < kSub; s++)
+      if (s * kSubElems < n && !mbar_wait(&bar[s], 0, kWaitCycles)) timed_out = 1;
+  if (__syncthreads_or(timed_out)) {
+    // the call fails (status word = this call's epoch; the resolve kernel
+    // reports -1); let any copy still in flight land (bounded) and stop
+    if (tid == 0) {
+      atomicExch(A.status, A.epoch);
+      for (int s = 0; s < kSub; s++)
+        if (s * kSubElems < n) mbar_wait(&bar[s], 0, kWaitCycles);
     }
+    __syncthreads();
+    return;
+  }
+  // phase 1: which of this thread's elements fall in each range (bit 4i + l:
+  // element l of its float4 i), and how many lie above each range
+  const float4* t4 = reinterpret_cast<const float4*>(tile);
+  constexpr int kIt = kChunk / 4 / kThreads;  // 8 float4 per thread
+  static_assert(4 * kIt <= 32, "hit bits fit one word");
+  auto pen_x = [&](float x, int j) {
+    return (PEN && ((penmask[j >> 5] >> (j & 31)) & 1u)) ? pen_apply_fast(x, A.pen, A.rpen) : x;
   };
-  float cur[4], nxt[4];
-  load4(4 * tid, cur);
+  uint32_t m0 = 0, m1 = 0;
   int above0 = 0, above1 = 0;
-  for (int rd = 0; rd < rounds; rd++) {
-    const int j0 = 4 * (rd * (int)blockDim.x + tid);
-    if (rd + 1 < rounds) load4(j0 + step, nxt);  // next round in flight
-    uint32_t in0 = 0, in1 = 0;
+  const bool two = nr > 1;
+#pragma unroll
+  for (int i = 0; i < kIt; i++) {
+    const int q = tid + i * kThreads;
+    const float4 v = t4[q];
+    const float xs[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int l = 0; l < 4; l++) {
-      float x = cur[l];
-      const int j = j0 + l;
-      if (PEN && j < n && ((penmask[j >> 5] >> (j & 31)) & 1u)) {
-        x = pen_apply_fast(x, A.pen, A.rpen);
-        cur[l] = x;
-      }
-      const float w = __fmul_rn(-x, a16);  // NaN (padding, or a NaN row) fails every test
-      in0 |= (uint32_t)(w >= flo[0] && w < fhi[0]) << l;
-      in1 |= (uint32_t)(w >= flo[1] && w < fhi[1]) << l;
+      const float w = __fmul_rn(-pen_x(xs[l], 4 * q + l), a16);  // NaN (padding, a NaN row) fails every test
+      const bool ge0 = w >= flo[0];
+      m0 |= (uint32_t)(ge0 && w < fhi[0]) << (4 * i + l);
       above0 += w < flo[0];
-      above1 += w < flo[1];
-    }
-    if (__any_sync(kAll, (in0 | in1) != 0)) {
-      // slots for this round's elements: one atomic per list per warp
-      const int c0n = __popc(in0), c1n = __popc(in1);
-      int s0 = c0n, s1 = c1n;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t0 = __shfl_up_sync(kAll, s0, o), t1 = __shfl_up_sync(kAll, s1, o);
-        if (lane >= o) { s0 += t0; s1 += t1; }
-      }
-      int b0 = 0, b1 = 0;
-      if (lane == 31) {
-        if (s0) b0 = atomicAdd(&A.list_cnt[4 * r], s0);
-        if (s1) b1 = atomicAdd(&A.list_cnt[4 * r + 1], s1);
-      }
-      b0 = __shfl_sync(kAll, b0, 31) + s0 - c0n;
-      b1 = __shfl_sync(kAll, b1, 31) + s1 - c1n;
-#pragma unroll
-      for (int l = 0; l < 4; l++) {
-        if ((in0 >> l) & 1u) { if (b0 < kListCap) out0[b0] = Cand{cur[l], c0 + j0 + l}; b0++; }
-        if ((in1 >> l) & 1u) { if (b1 < kListCap) out1[b1] = Cand{cur[l], c0 + j0 + l}; b1++; }
+      if (two) {
+        m1 |= (uint32_t)(w >= flo[1] && w < fhi[1]) << (4 * i + l);
+        above1 += w < flo[1];
       }
     }
+  }
+  // phase 2: one slot allocation per list per CTA, then each thread writes its hits
+  __shared__ int sbase[2];
+  const int packed = __popc(m0) | (__popc(m1) << 16);  // at most 32 each: no carry between halves
+  int incl = packed;
 #pragma unroll
-    for (int l = 0; l < 4; l++) cur[l] = nxt[l];
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(kAll, incl, o);
+    if (lane >= o) incl += t;
+  }
+  __shared__ int wtot[kThreads / 32];
+  if (lane == 31) wtot[tid >> 5] = incl;
+  __syncthreads();
+  if (tid < 32) {
+    int v = tid < kThreads / 32 ? wtot[tid] : 0;
+    int vi = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(kAll, vi, o);
+      if (tid >= o) vi += t;
+    }
+    if (tid < kThreads / 32) wtot[tid] = vi - v;  // exclusive over warps
+    if (tid == 31) {
+      const int t0 = vi & 0xFFFF, t1 = vi >> 16;
+      sbase[0] = t0 ? atomicAdd(&A.list_cnt[4 * r], t0) : 0;
+      sbase[1] = t1 ? atomicAdd(&A.list_cnt[4 * r + 1], t1) : 0;
+    }
+  }
+  __syncthreads();
+  const int excl = wtot[tid >> 5] + incl - packed;
+  int b0 = sbase[0] + (excl & 0xFFFF), b1 = sbase[1] + (excl >> 16);
+  Cand* out0 = A.lists + (int64_t)(2 * r) * kListCap;
+  Cand* out1 = out0 + kListCap;
+  for (uint32_t mm = m0; mm; mm &= mm - 1u) {
+    const int bit = __ffs(mm) - 1, j = 4 * (tid + (bit >> 2) * kThreads) + (bit & 3);
+    if (b0 < kListCap) out0[b0] = Cand{pen_x(tile[j], j), c0 + j};
+    b0++;
+  }
+  for (uint32_t mm = m1; mm; mm &= mm - 1u) {
+    const int bit = __ffs(mm) - 1, j = 4 * (tid + (bit >> 2) * kThreads) + (bit & 3);
+    if (b1 < kListCap) out1[b1] = Cand{pen_x(tile[j], j), c0 + j};
+    b1++;
   }
   above0 = __reduce_add_sync(kAll, above0);
   above1 = __reduce_add_sync(kAll, above1);
@@ -387,15 +433,20 @@ __global__ void __launch_bounds__(256) nucleus_extract_kernel(const __grid_const
 }
 
 // =============================================================== resolve
+constexpr int kListCache = 4096;  // extracted elements a resolve CTA keeps in shared memory
+
 struct ResSmem {
-  float prob[kListCap];                // exact probabilities of the list
+  Cand cache[kListCache];              // the range's elements, when they fit
   int scnt[kNSB];                      // sub-bin counts
-  uint32_t smlo[kNSB], smhi[kNSB];     // sub-bin masses, 2^-60 units
+  uint32_t smlo[kNSB], smhi[kNSB];     // sub-bin fast masses, 2^-60 units
   unsigned long long key[kExtCap];     // the crossing sub-bin's (prob desc, id asc) keys
   long long red_c[32];
   double red_d[32];
   uint32_t kmin, kmax;
   int sel, n_key, found;
+  long long gt_c;
+  uint32_t gt_lo, gt_hi;
+  float tl, th;
   long long rank_before;
   double mass_before;
   int out_id;
@@ -404,28 +455,51 @@ struct ResSmem {
 };
 constexpr double kTwo60 = 1152921504606846976.0;
 
-// In one extracted range (m elements, cnt_above / mass_above the elements and
-// fast mass of the bins above it), the first element in (prob desc, id asc)
-// order where rank >= rank_target or the running mass >= mass_target (either
-// may be disabled: rank_target <= 0, mass_target NaN).  One CTA; returns false
-// when the elements or the sub-bin cannot settle it.
-__device__ bool select_in_list(const Args& A, const Cand* L, int m, long long cnt_above, double mass_above,
-                               long long rank_target, double mass_target, float Mp, double S, ResSmem& R,
-                               int* id, long long* rank, double* cum) {
-  const int tid = threadIdx.x, nt = (int)blockDim.x;
+__device__ __forceinline__ void add_mass60(uint32_t* lo, uint32_t* hi, double mass) {
+  const unsigned long long u = (unsigned long long)(mass * kTwo60);
+  const uint32_t l = (uint32_t)u, h = (uint32_t)(u >> 32);
+  const uint32_t old = atomicAdd(lo, l);
+  const uint32_t up = h + ((old + l < old) ? 1u : 0u);
+  if (up) atomicAdd(hi, up);
+}
+
+// In one extracted range (m elements; cnt_above / mass_above the elements and
+// fast probability mass of the row above it), the first element in
+// (prob desc, id asc) order where rank >= rank_target or the running mass
+// >= mass_target (either may be disabled: rank_target <= 0, mass_target NaN).
+// Sub-bins of the range's logits (fast masses) find the crossing sub-bin; it
+// is widened to whole probability-tie groups, whose elements alone get exact
+// probabilities and keys; the mass above them stays fast, as in full_path.
+// The range covers -x * a16 in [wlo, whi): a tie group reaching past it holds
+// elements that were not extracted, and the row is not settled here.
+// One CTA; false when the range or the sub-bin cannot settle it.
+__device__ bool select_in_list(const Args& A, const RowInfo& Ri, const Cand* L, int m, float wlo, float whi,
+                               long long cnt_above, double mass_above, long long rank_target, double mass_target,
+                               ResSmem& R, int* id, long long* rank, double* cum) {
+  const int tid = threadIdx.x, nt = (int)blockDim.x, warp = tid >> 5;
   // a target reached before the range, or an empty range, is not settled here
   if (m <= 0 || (rank_target > 0 && cnt_above >= rank_target) || (mass_target == mass_target && mass_above >= mass_target))
     return false;
-  if (tid == 0) { R.kmin = 0xFFFFFFFFu; R.kmax = 0u; R.found = 0; R.n_key = 0; R.sel = -1; }
+  auto reached = [&](long long c, double mm) {
+    return (rank_target > 0 && c >= rank_target) || (mass_target == mass_target && mm >= mass_target);
+  };
+  const bool cached = m <= kListCache;  // the first pass copies the range into shared memory
+  auto gload = [&](int j) {
+    const float2 cv = __ldcg(reinterpret_cast<const float2*>(L + j));
+    return Cand{cv.x, __float_as_int(cv.y)};
+  };
+  auto load = [&](int j) { return cached ? R.cache[j] : gload(j); };
+  if (tid == 0) {
+    R.kmin = 0xFFFFFFFFu; R.kmax = 0u; R.found = 0; R.n_key = 0; R.sel = kNSB;
+    R.gt_c = 0; R.gt_lo = 0u; R.gt_hi = 0u;
+  }
   for (int b = tid; b < kNSB; b += nt) { R.scnt[b] = 0; R.smlo[b] = 0u; R.smhi[b] = 0u; }
   __syncthreads();
   uint32_t kmn = 0xFFFFFFFFu, kmx = 0u;
   for (int j = tid; j < m; j += nt) {
-    const float2 cv = __ldcg(reinterpret_cast<const float2*>(L + j));
-    const Cand cd{cv.x, __float_as_int(cv.y)};
-    const float p = prob_exact(term_exact(temper_fast(cd.x, A.T, A.rT, A.temper), Mp), S);
-    R.prob[j] = p;
-    const uint32_t k = __float_as_uint(p);  // p >= 0: bits grow with p
+    const Cand cd = gload(j);
+    if (cached) R.cache[j] = cd;
+    const uint32_t k = fkey(cd.x);
     kmn = min(kmn, k);
     kmx = max(kmx, k);
   }
@@ -433,65 +507,61 @@ __device__ bool select_in_list(const Args& A, const Cand* L, int m, long long cn
   kmx = __reduce_max_sync(kAll, kmx);
   if ((tid & 31) == 0) { atomicMin(&R.kmin, kmn); atomicMax(&R.kmax, kmx); }
   __syncthreads();
-  const uint32_t kmin = R.kmin, kmax = R.kmax;
-  const unsigned long long span = (unsigned long long)(kmax - kmin) + 1ull;
-  auto sub = [&](float p) {  // sub-bin 0 holds the largest probabilities
-    return (int)(((unsigned long long)(kmax - __float_as_uint(p)) * kNSB) / span);
-  };
+  const uint32_t kmax = R.kmax;
+  const unsigned long long span = (unsigned long long)(kmax - R.kmin) + 1ull;
+  auto sub = [&](uint32_t k) { return (int)(((unsigned long long)(kmax - k) * kNSB) / span); };  // 0: largest x
   for (int j = tid; j < m; j += nt) {
-    const float p = R.prob[j];
-    const int b = sub(p);
+    const float x = load(j).x;
+    const int b = sub(fkey(x));
     atomicAdd(&R.scnt[b], 1);
-    const unsigned long long u = (unsigned long long)((double)p * kTwo60);
-    const uint32_t lo = (uint32_t)u, hi = (uint32_t)(u >> 32);
-    const uint32_t old = atomicAdd(&R.smlo[b], lo);
-    const uint32_t up = hi + ((old + lo < old) ? 1u : 0u);
-    if (up) atomicAdd(&R.smhi[b], up);
+    add_mass60(&R.smlo[b], &R.smhi[b], mass_fast(Ri, x));
   }
   __syncthreads();
-  // prefix over the sub-bins (two per thread with kNB = 512 threads)
+  // prefix over the sub-bins (two per thread: kNSB == 2 * blockDim.x)
   long long c2[2];
   double m2[2];
 #pragma unroll
   for (int q = 0; q < 2; q++) {
     const int b = 2 * tid + q;
-    c2[q] = b < kNSB ? R.scnt[b] : 0;
-    m2[q] = b < kNSB ? ((double)R.smhi[b] * 4294967296.0 + (double)R.smlo[b]) * (1.0 / kTwo60) : 0.0;
+    c2[q] = R.scnt[b];
+    m2[q] = ((double)R.smhi[b] * 4294967296.0 + (double)R.smlo[b]) * (1.0 / kTwo60);
   }
   const long long cs = block_incl_scan<long long>(c2[0] + c2[1], R.red_c);
   const double msum = block_incl_scan<double>(m2[0] + m2[1], R.red_d);
-  // the first sub-bin whose end reaches a target (it holds the element sought;
-  // an empty one means the target lies before this range)
-  if (tid == 0) R.sel = kNSB;
-  __syncthreads();
-  auto reached = [&](long long c, double mm) {
-    return (rank_target > 0 && c >= rank_target) || (mass_target == mass_target && mm >= mass_target);
-  };
 #pragma unroll
-  for (int q = 0; q < 2; q++) {
-    const int b = 2 * tid + q;
-    const long long cend = cnt_above + cs - (q == 0 ? c2[1] : 0);
-    const double mend = mass_above + msum - (q == 0 ? m2[1] : 0.0);
-    if (b < kNSB && reached(cend, mend)) atomicMin(&R.sel, b);
-  }
+  for (int q = 0; q < 2; q++)
+    if (reached(cnt_above + cs - (q == 0 ? c2[1] : 0), mass_above + msum - (q == 0 ? m2[1] : 0.0)))
+      atomicMin(&R.sel, 2 * tid + q);
   __syncthreads();
   const int sel = R.sel;
   if (sel >= kNSB) return false;  // the targets lie beyond this range
-  if ((sel >> 1) == tid) {        // the totals before the selected sub-bin
-    const int q = sel & 1;
-    R.rank_before = cnt_above + cs - c2[1] - (q == 0 ? c2[0] : 0);
-    R.mass_before = mass_above + msum - m2[1] - (q == 0 ? m2[0] : 0.0);
+  // the selected sub-bin's key interval, widened to whole probability-tie groups
+  if (warp == 0) {
+    const unsigned long long d0 = ((unsigned long long)sel * span + kNSB - 1) / kNSB;
+    const unsigned long long d1 = ((unsigned long long)(sel + 1) * span + kNSB - 1) / kNSB - 1;
+    const float xhi = fkey_inv((uint32_t)(kmax - d0)), xlo = fkey_inv((uint32_t)(kmax - d1));
+    const float tl = tie_low(Ri, xlo), th = tie_high(Ri, xhi);
+    if ((tid & 31) == 0) { R.tl = tl; R.th = th; }
   }
   __syncthreads();
-  // its elements, ranked exactly
+  const float tl = R.tl, th = R.th;
+  const float a16 = __fmul_rn(A.a, 16.f);
+  if (!(__fmul_rn(-th, a16) >= wlo) || !(__fmul_rn(-tl, a16) < whi)) return false;
+  long long gc = 0;
   for (int j = tid; j < m; j += nt) {
-    const float p = R.prob[j];
-    if (sub(p) == sel) {
+    const Cand cd = load(j);
+    if (cd.x > th) {
+      gc++;
+      add_mass60(&R.gt_lo, &R.gt_hi, mass_fast(Ri, cd.x));
+    } else if (cd.x >= tl) {
       const int q = atomicAdd(&R.n_key, 1);
       if (q < kExtCap)
-        R.key[q] = ((unsigned long long)(0xFFFFFFFFu - __float_as_uint(p)) << 32) | (uint32_t)__ldcg(&L[j].i);
+        R.key[q] = ((unsigned long long)(0xFFFFFFFFu - __float_as_uint(prob_of(Ri, cd.x))) << 32) | (uint32_t)cd.i;
     }
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) gc += __shfl_xor_sync(kAll, gc, o);
+  if ((tid & 31) == 0 && gc) atomicAdd(reinterpret_cast<unsigned long long*>(&R.gt_c), (unsigned long long)gc);
   __syncthreads();
   const int nk = R.n_key;
   if (nk > kExtCap) return false;
@@ -512,13 +582,13 @@ __device__ bool select_in_list(const Args& A, const Cand* L, int m, long long cn
     }
   }
   if (tid == 0) {
-    long long rk = R.rank_before;
-    double acc = R.mass_before;
+    long long rk = cnt_above + R.gt_c;
+    double acc = mass_above + ((double)R.gt_hi * 4294967296.0 + (double)R.gt_lo) * (1.0 / kTwo60);
     int hit = -1;
     for (int i = 0; i < nk; i++) {
       rk++;
       acc += (double)__uint_as_float(0xFFFFFFFFu - (uint32_t)(R.key[i] >> 32));
-      if ((rank_target > 0 && rk >= rank_target) || (mass_target == mass_target && acc >= mass_target)) {
+      if (reached(rk, acc)) {
         hit = i;
         break;
       }
@@ -551,57 +621,12 @@ __global__ void __launch_bounds__(kNB, 2) nucleus_resolve_kernel(const __grid_co
   const int r = blockIdx.x, tid = threadIdx.x, nt = (int)blockDim.x;
   const NucPlan pl = A.plan[r];
   if (pl.flags == kPlanDone) return;
-  const bool use_k = A.k > 0 && A.k < A.V;
-  bool ok = pl.flags == 0;
-  int out_id = -1;
-  long long n = use_k ? A.k : A.V;
-  double total = pl.mass_tot;
-  int last_id = -1;
-  const bool counts = A.h_cnt != nullptr;
-  // a list that overflowed cannot settle the row; without histogram counts the
-  // extraction counted the elements above each range
-  for (int k = 0; k < pl.nr; k++)
-    if (__ldcg(&A.list_cnt[4 * r + k]) > kListCap) ok = false;
-  long long above[2];
-  for (int k = 0; k < 2; k++) above[k] = counts ? pl.cnt_above[k] : (long long)__ldcg(&A.list_cnt[4 * r + 2 + k]);
-  if (ok && pl.cut_rg >= 0) {
-    const int k = pl.cut_rg;
-    const int m = min(__ldcg(&A.list_cnt[4 * r + k]), kListCap);
-    const double mt = (A.use_topp && A.top_p >= 0.0) ? A.top_p : __longlong_as_double(0x7ff8000000000000ll);
-    const long long rt = A.use_topp && A.top_p < 0.0 ? 1 : (use_k ? (long long)A.k : 0);
-    int id;
-    long long rk;
-    double cum;
-    ok = select_in_list(A, A.lists + (int64_t)(2 * r + k) * kListCap, m, above[k], pl.mass_above[k], rt, mt,
-                        pl.Mp, pl.S, R, &id, &rk, &cum);
-    if (ok) {
-      n = rk;
-      total = cum;
-      last_id = id;
+  if (*((volatile int32_t*)A.status) == A.epoch) {  // a wait of this call ran out
+    if (tid == 0) {
+      A.out_ids[r] = -1;
+      if (A.d_row_flags) A.d_row_flags[r] = MS_ROW_TIMEOUT;
     }
-  }
-  if (ok) {
-    const double u = A.u ? A.u[r] : 0.0;
-    const double rr = u * total;
-    const int k = pl.draw_rg;
-    const int m = min(__ldcg(&A.list_cnt[4 * r + k]), kListCap);
-    int id;
-    long long rk;
-    double cum;
-    if (rr <= 0.0 || rr != rr)
-      ok = rr == rr && select_in_list(A, A.lists + (int64_t)(2 * r + k) * kListCap, m, above[k], pl.mass_above[k],
-                                      1, __longlong_as_double(0x7ff8000000000000ll), pl.Mp, pl.S, R, &id, &rk,
-                                      &cum);
-    else
-      ok = select_in_list(A, A.lists + (int64_t)(2 * r + k) * kListCap, m, above[k], pl.mass_above[k], 0, rr,
-                          pl.Mp, pl.S, R, &id, &rk, &cum);
-    if (ok) {
-      if (rk > n) {  // past the cut: the reference's loop ends on the last candidate
-        ok = last_id >= 0;
-        id = last_id;
-      }
-      out_id = id;
-    }
+    return;
   }
   RowInfo Ri;
   Ri.row = A.logits + (int64_t)r * A.ld;
@@ -617,6 +642,65 @@ __global__ void __launch_bounds__(kNB, 2) nucleus_resolve_kernel(const __grid_co
   Ri.T = A.T;
   Ri.temper = A.temper;
   Ri.nat16 = (float)(16.0 / A.T);
+  Ri.rT = A.rT;
+  Ri.rS = 1.0 / Ri.S;
+  const bool use_k = A.k > 0 && A.k < A.V;
+  bool ok = pl.flags == 0;
+  int out_id = -1;
+  long long n = use_k ? A.k : A.V;
+  double total = pl.mass_tot;
+  int last_id = -1;
+  const bool counts = A.h_cnt != nullptr;
+  // a list that overflowed cannot settle the row; without histogram counts the
+  // extraction counted the elements above each range
+  for (int k = 0; k < pl.nr; k++)
+    if (__ldcg(&A.list_cnt[4 * r + k]) > kListCap) ok = false;
+  long long above[2];
+  float wlo[2], whi[2];  // each range as the interval of -x * a16 it covers
+  for (int k = 0; k < 2; k++) {
+    above[k] = counts ? pl.cnt_above[k] : (long long)__ldcg(&A.list_cnt[4 * r + 2 + k]);
+    wlo[k] = (float)(pl.b_row + pl.lo[k]);
+    whi[k] = pl.hi[k] >= kNB - 1 ? INFINITY : (float)(pl.b_row + pl.hi[k] + 1);
+  }
+  if (ok && pl.cut_rg >= 0) {
+    const int k = pl.cut_rg;
+    const int m = min(__ldcg(&A.list_cnt[4 * r + k]), kListCap);
+    const double mt = (A.use_topp && A.top_p >= 0.0) ? A.top_p : __longlong_as_double(0x7ff8000000000000ll);
+    const long long rt = A.use_topp && A.top_p < 0.0 ? 1 : (use_k ? (long long)A.k : 0);
+    int id;
+    long long rk;
+    double cum;
+    ok = select_in_list(A, Ri, A.lists + (int64_t)(2 * r + k) * kListCap, m, wlo[k], whi[k], above[k], pl.mass_above[k], rt, mt,
+                        R, &id, &rk, &cum);
+    if (ok) {
+      n = rk;
+      total = cum;
+      last_id = id;
+    }
+  }
+  if (ok) {
+    const double u = A.u ? A.u[r] : 0.0;
+    const double rr = u * total;
+    const int k = pl.draw_rg;
+    const int m = min(__ldcg(&A.list_cnt[4 * r + k]), kListCap);
+    int id;
+    long long rk;
+    double cum;
+    if (rr <= 0.0 || rr != rr)
+      ok = rr == rr && select_in_list(A, Ri, A.lists + (int64_t)(2 * r + k) * kListCap, m, wlo[k], whi[k], above[k],
+                                      pl.mass_above[k], 1, __longlong_as_double(0x7ff8000000000000ll), R, &id, &rk,
+                                      &cum);
+    else
+      ok = select_in_list(A, Ri, A.lists + (int64_t)(2 * r + k) * kListCap, m, wlo[k], whi[k], above[k], pl.mass_above[k], 0, rr, R,
+                          &id, &rk, &cum);
+    if (ok) {
+      if (rk > n) {  // past the cut: the reference's loop ends on the last candidate
+        ok = last_id >= 0;
+        id = last_id;
+      }
+      out_id = id;
+    }
+  }
   const bool diag_cands = (A.d_cand_ids || A.d_cand_probs) && A.cand_cap > 0;
   if ((!ok || diag_cands) && A.use_pen && A.penbits) {  // the exact path reads penalised values through a bitmap
     const int W = (A.V + 31) >> 5;
