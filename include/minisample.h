@@ -185,6 +185,23 @@ int ms_profile_read(ms_ctx* ctx, double* stream_ms, double* finalize_ms, int64_t
 int ms_launch_count(ms_ctx* ctx, int64_t* kernels);
 
 /*
+ * Keeps a generation loop's penalty history on the device.  Replaces the
+ * reference's per-step history `inputIds.concat(generated)` (src/generation.js:
+ * 73-74, grown by `generated.push(nextId)` at :105): instead of uploading it
+ * every step, the caller keeps a [B, cap] int32 device buffer `hist` whose row r
+ * holds the row's ids in hist[r*cap .. r*cap + len[r]) and -1 in the rest, and
+ * passes it to ms_sample with hist_off[r] = r*cap (ids outside [0, V) are
+ * ignored by the penalty, so the -1 slots change nothing).  This call appends
+ * ids[r] to row r (ids < 0 are skipped; a full row, len[r] == cap, drops the id:
+ * size cap for the prompt plus every generated id).  Device pointers, on
+ * `stream` (NULL = the ctx stream), on the context's first device; asynchronous.
+ * As in the reference, the penalty starts once something was generated: pass
+ * no history to the first ms_sample call of a generation.
+ */
+int ms_history_append(ms_ctx* ctx, int32_t* hist, int32_t* len, int64_t B, int64_t cap, const int32_t* ids,
+                      void* stream);
+
+/*
  * Bytes of device scratch that ms_sample needs for a [B, V] call with these
  * params (the context allocates it on first use and keeps it).
  */

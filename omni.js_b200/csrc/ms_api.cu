@@ -18,6 +18,8 @@ cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev, i
 cudaError_t launch_shard(const Args& A, cudaStream_t stream);
 cudaError_t launch_merge(const Args& A, cudaStream_t stream);
 cudaError_t launch_exp(const double* x, double* y, int64_t n, cudaStream_t stream);
+cudaError_t launch_history_append(int32_t* hist, int32_t* len, int64_t B, int64_t cap, const int32_t* ids,
+                                  cudaStream_t stream);
 size_t finalize_smem_bytes();
 }  // namespace ms
 
@@ -325,6 +327,21 @@ int ms_debug_inject(ms_ctx* c, int what, int64_t arg) {
   if (what == MS_INJECT_WAIT) c->inject_wait = (long long)arg;
   else if (what == MS_INJECT_ALLOC) c->inject_alloc = arg != 0;
   else return fail(c, MS_ERR_ARG, "ms_debug_inject: unknown injection %d", what);
+  return MS_OK;
+}
+
+int ms_history_append(ms_ctx* c, int32_t* hist, int32_t* len, int64_t B, int64_t cap, const int32_t* ids,
+                      void* stream) {
+  if (!c) return MS_ERR_ARG;
+  if (B < 0 || cap < 1 || cap > INT32_MAX) return fail(c, MS_ERR_ARG, "ms_history_append: bad B / cap");
+  if (B == 0) return MS_OK;
+  if (!hist || !len || !ids) return fail(c, MS_ERR_ARG, "ms_history_append: NULL pointer");
+  if ((uint64_t)B * (uint64_t)cap > (uint64_t)INT64_MAX / 4) return fail(c, MS_ERR_ARG, "ms_history_append: too large");
+  DevState& s = c->devs[0];
+  MS_CUDA(c, cudaSetDevice(s.device));
+  cudaStream_t st = stream ? (cudaStream_t)stream : s.stream;
+  MS_CUDA(c, ms::launch_history_append(hist, len, B, cap, ids, st));
+  s.launches += 1;
   return MS_OK;
 }
 

@@ -323,7 +323,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
                : "memory");
 }
-// Untiled TMA bulk copy global -> shared (no multicast).  dst, src 16-byte
+// Untiled TMA bulk copy global -> shared, one destination CTA.  dst, src 16-byte
 // aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

@@ -1332,6 +1332,25 @@ cudaError_t launch_merge(const Args& A, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// Appends ids[r] to row r's device history (hist[r * cap + len[r]], then
+// len[r] + 1); ids < 0 and full rows are skipped.
+__global__ void history_append_kernel(int32_t* hist, int32_t* len, int64_t B, int64_t cap, const int32_t* ids) {
+  const int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  if (r >= B) return;
+  const int32_t id = ids[r];
+  const int32_t n = len[r];
+  if (id < 0 || n < 0 || n >= cap) return;
+  hist[r * cap + n] = id;
+  len[r] = n + 1;
+}
+
+cudaError_t launch_history_append(int32_t* hist, int32_t* len, int64_t B, int64_t cap, const int32_t* ids,
+                                  cudaStream_t stream) {
+  const int64_t blocks = (B + 255) / 256;
+  history_append_kernel<<<(unsigned)blocks, 256, 0, stream>>>(hist, len, B, cap, ids);
+  return cudaGetLastError();
+}
+
 __global__ void exp_kernel(const double* x, double* y, int64_t n) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     y[i] = js_exp(x[i]);

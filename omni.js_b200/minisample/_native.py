@@ -48,7 +48,7 @@ ERROR_NAMES = {
 # Every symbol include/minisample.h declares.
 EXPORTED = ("ms_version", "ms_create", "ms_destroy", "ms_last_error", "ms_sample", "ms_profile_read",
             "ms_scratch_bytes", "ms_sample_noalloc", "ms_launch_count", "ms_shard_record_bytes",
-            "ms_shard_records", "ms_merge_records", "ms_debug_inject", "ms_debug_exp")
+            "ms_shard_records", "ms_merge_records", "ms_debug_inject", "ms_debug_exp", "ms_history_append")
 
 
 class MsParams(ctypes.Structure):
@@ -131,6 +131,9 @@ def load(path: str | None = None):
     L.ms_scratch_bytes.restype = ctypes.c_int
     L.ms_scratch_bytes.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.POINTER(MsParams),
                                    ctypes.POINTER(ctypes.c_int64)]
+    L.ms_history_append.restype = ctypes.c_int
+    L.ms_history_append.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64,
+                                    ctypes.c_void_p, ctypes.c_void_p]
     L.ms_debug_exp.restype = ctypes.c_int
     L.ms_debug_exp.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
     L.ms_debug_inject.restype = ctypes.c_int

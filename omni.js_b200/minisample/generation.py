@@ -198,3 +198,89 @@ def generate_tokens_batch(model, input_ids_batch, options=None, rands=None):
     finally:
         for i in range(B):
             models[i].dispose_cache(caches[i])
+
+
+class DeviceHistory:
+    """A batch's penalty histories kept on the GPU (ms_history_append).  Row r
+    holds its prompt and generated ids in hist[r, :lens[r]] and -1 after them
+    (the penalty ignores ids outside the vocabulary), so (hist, off) is a
+    ready CSR history for the sampler.  The prompts are uploaded once; each
+    step appends the sampled ids on the device (src/generation.js:73-74, 105)."""
+
+    def __init__(self, input_ids_batch, cap: int, device):
+        import torch
+
+        B = len(input_ids_batch)
+        h = np.full((B, cap), -1, np.int32)
+        lens = np.zeros(B, np.int32)
+        for i, ids in enumerate(input_ids_batch):
+            a = np.asarray(list(ids), dtype=np.int64)[:cap]
+            h[i, : a.shape[0]] = np.where((a < 0) | (a > 2**31 - 1), -1, a).astype(np.int32)
+            lens[i] = a.shape[0]
+        self.hist = torch.from_numpy(h).to(device)
+        self.lens = torch.from_numpy(lens).to(device)
+        self.off = torch.arange(0, (B + 1) * cap, cap, dtype=torch.int64, device=device)
+        self.upload_bytes = h.nbytes + lens.nbytes + self.off.numel() * 8
+
+    def append(self, sampler: Sampler, ids) -> None:
+        sampler.history_append(self.hist, self.lens, ids)
+
+
+def generate_tokens_device(model, input_ids_batch, options=None, rands=None):
+    """Batched generation with the logits and the penalty history on the GPU.
+
+    model.forward_batch(last_ids, caches) returns the [B, V] fp32 CUDA logits of
+    the next step for every row (last_ids is None for the prompts; the logits
+    come from the model's lm head on the device, so no logits cross the host
+    link); model.make_cache() / dispose_cache(cache) as in generate_tokens.  Each
+    step samples on the device, appends the ids to the device history, and
+    copies only the B ids back for the onToken / EOS rules, which are those of
+    generate_tokens_batch (per row, src/generation.js:97-114).  Rows that
+    stopped keep a slot in the batch; their ids are ignored and draw no
+    uniform.  Returns the generated ids of each row."""
+    import torch
+
+    opts = normalize_options(options)
+    B = len(input_ids_batch)
+    rands = rands if rands is not None else [_random.random] * B
+    on_token = opts["on_token"]
+    greedy = is_greedy(opts)
+    params = params_of(opts)
+    steps = int(opts["max_new_tokens"])
+    s = _sampler()
+    caches = [model.make_cache() for _ in range(B)]
+    try:
+        logits = model.forward_batch(None, caches)
+        dev = logits.device
+        cap = max(len(list(x)) for x in input_ids_batch) + max(steps, 1)
+        H = DeviceHistory(input_ids_batch, cap, dev)
+        ids_d = torch.empty(B, dtype=torch.int32, device=dev)
+        generated = [[] for _ in range(B)]
+        active = [True] * B
+        for step in range(steps):
+            if not any(active):
+                break
+            u = None
+            if not greedy:
+                u = torch.tensor([rands[i]() if active[i] else 0.0 for i in range(B)], dtype=torch.float64,
+                                 device=dev)
+            # the penalty starts once something was generated (src/generation.js:73)
+            hist = (H.hist.view(-1), H.off) if step > 0 else (None, None)
+            s.sample(logits, params, u=u, hist=hist[0], hist_off=hist[1], out=ids_d, sync=False)
+            H.append(s, ids_d)
+            ids = ids_d.cpu().numpy()
+            for i in range(B):
+                if not active[i]:
+                    continue
+                nid = int(ids[i])
+                generated[i].append(nid)
+                if on_token and on_token(i, nid, step + 1) is False:
+                    active[i] = False
+                elif opts["eos_token_id"] is not None and nid == opts["eos_token_id"]:
+                    active[i] = False
+            if step + 1 < steps and any(active):
+                logits = model.forward_batch([int(x) for x in ids], caches)
+        return generated
+    finally:
+        for c in caches:
+            model.dispose_cache(c)

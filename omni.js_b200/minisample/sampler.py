@@ -98,6 +98,17 @@ class Sampler:
         self._check(self._L.ms_profile_read(self._ctx, ctypes.byref(a), ctypes.byref(b), ctypes.byref(n)))
         return a.value, b.value, n.value
 
+    def history_append(self, hist, lens, ids, stream=None) -> None:
+        """Appends ids[r] to row r of a device history ([B, cap] int32, -1 in unused
+        slots) and bumps lens[r] (ms_history_append)."""
+        import torch
+
+        B, cap = hist.shape
+        st = stream if stream is not None else torch.cuda.current_stream(hist.device)
+        with torch.cuda.device(hist.device):
+            self._check(self._L.ms_history_append(self._ctx, hist.data_ptr(), lens.data_ptr(), B, cap, ids.data_ptr(),
+                                                  _stream_handle(st)))
+
     def inject(self, what: int, arg: int) -> None:
         """Failure injection for the next call (ms_debug_inject): N.MS_INJECT_WAIT
         with a cycle count, or N.MS_INJECT_ALLOC."""

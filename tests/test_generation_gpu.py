@@ -160,3 +160,77 @@ def test_generate_tokens_batch_matches_oracle_loop(oracle, case):
         if i in stop_at:
             want = want[: stop_at[i]]
         assert got[i] == want, (i, got[i], want)
+
+
+class StubDeviceModel:
+    """The batched, device-resident counterpart of StubModel: forward_batch
+    returns the [B, V] CUDA logits whose row i equals StubModel(seeds[i])'s
+    output for the same step and last id."""
+
+    def __init__(self, seeds, input_ids_batch):
+        self.rows = [StubModel(sd) for sd in seeds]
+        self.inputs = input_ids_batch
+        self.host_caches = None
+
+    def make_cache(self):
+        return {}
+
+    def dispose_cache(self, cache):
+        pass
+
+    def forward_batch(self, last_ids, caches):
+        import torch
+
+        if last_ids is None:
+            self.host_caches = [m.make_cache() for m in self.rows]
+            xs = [m.forward(list(self.inputs[i]), self.host_caches[i]) for i, m in enumerate(self.rows)]
+        else:
+            xs = [m.forward([last_ids[i]], self.host_caches[i]) for i, m in enumerate(self.rows)]
+        return torch.from_numpy(np.concatenate(xs)).cuda()
+
+
+@pytest.mark.parametrize("case", [0, 1, 2])
+def test_generate_tokens_device_matches_oracle_loop(oracle, case):
+    """Logits and penalty history on the GPU (ms_history_append): each row's
+    ids equal the oracle's generation loop on that row with the same uniform
+    stream, with per-row EOS / onToken stops."""
+    from minisample.generation import generate_tokens_device, set_backend
+
+    set_backend("cuda")
+    opts = dict(CASES[case])
+    inputs = [[1, 2, 3], [7], [4, 4, 4, 4], [9, 8]]
+    per_row = [_oracle_loop(oracle, StubModel(80 + i), inputs[i], opts, _mulberry(90 + i)[0])
+               for i in range(len(inputs))]
+    eos = per_row[1][2]
+    stop_at = {3: 2}
+
+    def on_token(row, tid, n):
+        return not (row in stop_at and n >= stop_at[row])
+
+    opts_b = dict(opts, eosTokenId=eos, onToken=on_token)
+    got = generate_tokens_device(StubDeviceModel([80 + i for i in range(len(inputs))], inputs), inputs, opts_b,
+                                 rands=[_mulberry(90 + i)[0] for i in range(len(inputs))])
+    for i in range(len(inputs)):
+        want = per_row[i]
+        if eos in want:
+            want = want[: want.index(eos) + 1]
+        if i in stop_at:
+            want = want[: stop_at[i]]
+        assert got[i] == want, (i, got[i], want)
+
+
+def test_history_append_rows():
+    """ms_history_append writes each id after the row's last one, skips -1 and
+    full rows."""
+    import torch
+
+    from minisample.generation import DeviceHistory, set_backend, _sampler
+
+    set_backend("cuda")
+    H = DeviceHistory([[5, 6], [], [1, 2, 3]], 3, torch.device("cuda", 0))
+    ids = torch.tensor([7, 8, 9], dtype=torch.int32, device="cuda")
+    H.append(_sampler(), ids)
+    H.append(_sampler(), torch.tensor([-1, 10, 11], dtype=torch.int32, device="cuda"))
+    torch.cuda.synchronize()
+    assert H.hist.cpu().numpy().tolist() == [[5, 6, 7], [8, 10, -1], [1, 2, 3]]
+    assert H.lens.cpu().numpy().tolist() == [3, 2, 3]
