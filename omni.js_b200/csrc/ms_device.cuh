@@ -346,16 +346,19 @@ __device__ __forceinline__ void cp_async_mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
-// Bounded wait on phase `parity`; false when ~`max_cycles` passed first.
+// Bounded wait on phase `parity`; false when ~`max_cycles` passed first.  Each
+// try_wait may suspend the thread for up to kSuspendNs (it resumes as soon as
+// the phase completes), so a waiting warp issues few instructions.
+constexpr uint32_t kSuspendNs = 100000u;
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long long max_cycles) {
   uint32_t a = smem_addr(bar);
   long long t0 = clock64();
   for (;;) {
     uint32_t done;
     asm volatile(
-        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
         : "=r"(done)
-        : "r"(a), "r"(parity)
+        : "r"(a), "r"(parity), "r"(kSuspendNs)
         : "memory");
     if (done) return true;
     if (clock64() - t0 > max_cycles) return false;

@@ -1,15 +1,18 @@
 // Sampler kernel for B200 (sm_100a).
 //
 // One sampling step over a [B, V] fp32 logits block is ONE launch of
-// sample_kernel, grid (ceil(V/16384), B), 512 threads, 64 KiB of shared memory
-// per CTA (3 CTAs per SM).  Each CTA owns one 16384-logit chunk of one row:
+// sample_kernel, grid (B, ceil(V/16384)), 256 threads for sampled rows (512 for
+// greedy ones), 64 KiB of shared memory per CTA (3 CTAs per SM).  Each CTA owns
+// one 16384-logit chunk of one row:
 //
 //   1. thread 0 starts four 16 KiB TMA bulk copies of the chunk into shared
-//      memory; meanwhile all threads turn the row's id history into a bitmap
-//      of the chunk's penalised ids (so repeated ids count once, the reference's
-//      Set, src/generation.js:20);
+//      memory; meanwhile all threads read the row's id history in 16-byte
+//      blocks and set the bits of the chunk's penalised ids in a bitmap (so
+//      repeated ids count once, the reference's Set, src/generation.js:20);
 //   2. the penalty is applied in shared memory to the flagged logits
-//      (src/generation.js:19-25);
+//      (src/generation.js:19-25), each by the thread that reads it in the
+//      streaming passes (the bitmap is laid out per thread), so no barrier
+//      separates it from them;
 //   3. pass A: chunk max and a threshold tau that at least top_k elements of
 //      the chunk reach (from the sorted per-thread maxima of every warp);
 //   4. pass B: fast fp32 sum of 2^((x - m) * log2(e)/T) and the list of
@@ -40,7 +43,6 @@ namespace ms {
 
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s: bound on every wait
 constexpr unsigned kAll = 0xffffffffu;
-constexpr int kWarps = kThreads / 32;
 constexpr int kFinChunks = 256;  // chunks whose scale the finalizer caches
 
 // =============================================================== shared scratch
@@ -50,7 +52,7 @@ struct FinSmem {
   unsigned long long keys[kFinMax];  // the boundary bucket of the selection
   unsigned long long top[kKmax];     // the selected top_k keys
   int h1[256], h2[256];              // selection histograms
-  int b1, b2, need, n_lt, n_bkt, n_top;
+  int b1, b2, need, n_keep, n_bkt, n_top;
   int off[33];                       // merge: list offsets of the shards
   uint32_t kx;                       // kth_largest_x: the selected key
   int nf, nF, slow, nan_row, bad, overflow;
@@ -384,6 +386,64 @@ __device__ void gather_cands(const Args& A, int r, FinSmem& F) {
   __syncthreads();
 }
 
+// Narrows the nfc gathered candidates (all x >= tau_row, M the row max) to
+// those that can still be among the top k: a 256-bin histogram of x over
+// [tau_row, M] (per-warp copies in F.keys, so few lanes meet on one counter)
+// finds the bin holding the k-th largest x; the candidates of that bin and the
+// bins above it move to the front of F.gath.  Returns the new count, or nfc
+// when nothing is narrowed, and sets *xout to the largest x left out (-inf:
+// none).  F.h1, F.h2, F.n_top, F.n_bkt are zero again on return.  Ends with a
+// barrier.
+__device__ int narrow_cands(FinSmem& F, int nfc, int k, float tau_row, float M, float* xout) {
+  const int tid = threadIdx.x, warp = tid >> 5, nt = (int)blockDim.x;
+  *xout = -INFINITY;
+  const float span = M - tau_row;
+  // nothing to gain, or no finite range to bin over (uniform across the CTA)
+  if (nfc <= 2 * k || !(span > 0.f) || !(span <= FLT_MAX)) return nfc;
+  const float inv_w = 256.f / span;
+  auto bin = [&](float x) { return min(255, max(0, __float2int_rd(__fmul_rn(__fsub_rn(x, tau_row), inv_w)))); };
+  int* wh = reinterpret_cast<int*>(F.keys);  // 8 histograms of 256 bins
+  for (int b = tid; b < 8 * 256; b += nt) wh[b] = 0;
+  if (tid == 0) { F.n_keep = 0; F.kx = 0u; }
+  __syncthreads();
+  int* myh = wh + (warp & 7) * 256;
+  for (int j = tid; j < nfc; j += nt) atomicAdd(&myh[bin(F.gath[j].x)], 1);
+  __syncthreads();
+  // bins in descending x: F.h1[255 - b] counts bin b
+  for (int b = tid; b < 256; b += nt) {
+    int t = 0;
+#pragma unroll
+    for (int w = 0; w < 8; w++) t += wh[w * 256 + b];
+    F.h1[255 - b] = t;
+  }
+  __syncthreads();
+  if (warp == 0) scan_pick(F.h1, k, &F.b1, &F.need);
+  __syncthreads();
+  const int bk = 255 - F.b1;  // the bin of the k-th largest x: keep bins >= bk
+  Cand* keep = reinterpret_cast<Cand*>(F.top);  // room for kKmax candidates
+  for (int j = tid; j < nfc; j += nt) {
+    const Cand cd = F.gath[j];
+    if (bin(cd.x) >= bk) {
+      const int q = atomicAdd(&F.n_keep, 1);
+      if (q < kKmax) keep[q] = cd;
+    } else {
+      atomicMax(&F.kx, fkey(cd.x));
+    }
+  }
+  __syncthreads();
+  const int nk = F.n_keep;
+  const uint32_t kx = F.kx;
+  if (nk <= kKmax) {
+    for (int j = tid; j < nk; j += nt) F.gath[j] = keep[j];
+  }
+  for (int b = tid; b < 256; b += nt) { F.h1[b] = 0; F.h2[b] = 0; }
+  if (tid == 0) { F.n_top = 0; F.n_bkt = 0; }
+  __syncthreads();
+  if (nk > kKmax) return nfc;
+  *xout = kx ? fkey_inv(kx) : -INFINITY;
+  return nk;
+}
+
 template <int MODE>
 __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -440,12 +500,16 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   // ---- gather the candidates >= tau_row (all of them unless a chunk overflowed)
   gather_cands(A, r, F);
   const int nf = F.nf;
-  const int nfc = min(nf, kGathMax);
+  int nfc = min(nf, kGathMax);
   if (nf > kGathMax || (MODE == kTopK && nf < A.k)) {
     if (tid == 0) F.slow = 1;
   }
+  // ---- top-k rows: only the candidates that can reach the top k go on (the
+  // largest x left out bounds every probability outside them)
+  float xout = -INFINITY;
+  if (MODE == kTopK && nf <= kGathMax && nf >= A.k) nfc = narrow_cands(F, nfc, A.k, tau_row, M, &xout);
 
-  // ---- exact terms of every gathered candidate (kept in place of x) and the
+  // ---- exact terms of every remaining candidate (kept in place of x) and the
   // fast sum's correction: exact minus fast term, summed in 2^-50 units
   {
     long long corr = 0;
@@ -485,14 +549,15 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   R.rS = 1.0 / R.S;
 
   if (MODE == kTopK && !F.slow) {
-    // every element outside the candidates has x < tau_row, so its probability
-    // is at most that of the fp32 value below tau_row
+    // every element outside the candidates has x <= xout (a narrowed-out
+    // candidate) or x < tau_row, so its probability is at most that of xout or
+    // of the fp32 value below tau_row
     const double rS = 1.0 / S;
     if (tid == 0) {
       float po = -1.f;
-      if (tau_row != -INFINITY) {
-        const float below = fkey_inv(fkey(tau_row) - 1u);
-        po = div_to_f32((double)term_exact(temper_fast(below, A.T, A.rT, A.temper), Mp), S, rS);
+      if (xout != -INFINITY || tau_row != -INFINITY) {
+        const float xo = (xout != -INFINITY) ? xout : fkey_inv(fkey(tau_row) - 1u);
+        po = div_to_f32((double)term_exact(temper_fast(xo, A.T, A.rT, A.temper), Mp), S, rS);
       }
       F.pout = po;
     }
@@ -534,19 +599,76 @@ __device__ __forceinline__ int nuc_local(int bin, int top) {
 }
 
 // =============================================================== the kernel
+// The row's history ids (positions [h0, h1) of A.hist) that fall in chunk
+// [c0, c0 + n) set their bits in the chunk's penalty bitmap, so a repeated id
+// counts once (the reference's Set, src/generation.js:20).  The ids are read in
+// aligned 16-byte blocks: the first and the last block of the row may reach
+// past the row's ids (never past the 16-byte block holding one of them, so
+// never outside the buffer's pages) and those ids are masked off.
+//
+// Bit layouts: chunk position d is bit d of the bitmap (row-major), or, with
+// OWNER, the bit of the thread that reads d in the chunk kernel's streaming
+// loops: d lies in float4 q = d / 4, read by thread q % NT at step q / NT, and
+// its bit is 4 * (q / NT) + d % 4 of that thread's kChunk / NT bits (words
+// thread * kChunk / (32 * NT) onwards).
+template <int NT, bool OWNER>
+__device__ __forceinline__ void pen_scan(const Args& A, int64_t h0, int64_t h1, int c0, int n, uint32_t* penmask) {
+  constexpr int kWordsPerThread = kChunk / 32 / NT;
+  const int hn = (int)(h1 - h0);
+  if (hn <= 0) return;
+  const int32_t* hrow = A.hist + h0;
+  const int lead = (int)((reinterpret_cast<uintptr_t>(hrow) >> 2) & 3);  // ids of block 0 before the row
+  const int4* blk = reinterpret_cast<const int4*>(hrow - lead);
+  const int nb = (lead + hn + 3) >> 2;
+  const uint32_t base = (uint32_t)(A.col0 + c0);
+  for (int b = threadIdx.x; b < nb; b += NT) {
+    const int4 q = __ldg(blk + b);
+    const int e0 = 4 * b - lead;  // row position of q.x
+    // ids of the block inside the row: positions [max(0, -e0), min(4, hn - e0))
+    const uint32_t keep = (0xFu >> max(0, 4 - (hn - e0))) & (0xFu << max(0, -e0)) & 0xFu;
+    const uint32_t dd[4] = {(uint32_t)q.x - base, (uint32_t)q.y - base,   // ids outside the
+                            (uint32_t)q.z - base, (uint32_t)q.w - base};  // chunk wrap past n
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+      const uint32_t d = dd[k];
+      if ((keep & (1u << k)) && d < (uint32_t)n) {
+        if (OWNER) {
+          const uint32_t f4 = d >> 2, bit = ((f4 / NT) << 2) | (d & 3);
+          atomicOr(&penmask[(f4 % NT) * kWordsPerThread + (bit >> 5)], 1u << (bit & 31));
+        } else {
+          atomicOr(&penmask[d >> 5], 1u << (d & 31));
+        }
+      }
+    }
+  }
+}
+
+template <int NT>
+__device__ __forceinline__ void pen_bitmap(const Args& A, int r, int c0, int n, uint32_t* penmask) {
+  pen_scan<NT, false>(A, A.hist_off[r], A.hist_off[r + 1], c0, n, penmask);
+}
+
+// Threads of a chunk CTA.  Sampled rows take 256 (64 logits per thread: the
+// per-thread work outside the streaming loops is paid once per 64 logits);
+// greedy rows keep 512, since their CTAs also run the row finalize.
+template <int MODE>
+__host__ __device__ constexpr int chunk_threads() { return MODE == kGreedy ? kThreads : 256; }
+
 template <int MODE, bool PEN>
-__global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_constant__ Args A) {
+__global__ void __launch_bounds__(chunk_threads<MODE>(), 3) sample_kernel(const __grid_constant__ Args A) {
+  constexpr int NT = chunk_threads<MODE>(), NW = NT / 32;
+  constexpr int kPenWords = kChunk / 32 / NT;  // penalty bitmap words per thread
   extern __shared__ __align__(128) unsigned char dyn_smem[];
   float* tile = reinterpret_cast<float*>(dyn_smem);
   __shared__ __align__(8) uint64_t bar[kSub];
   __shared__ __align__(8) uint64_t stall_bar;  // test hook: an mbarrier nothing completes
-  __shared__ uint32_t penmask[kChunk / 32];
+  __shared__ uint32_t penmask[kChunk / 32];  // penalty bits, thread-major (pen_scan OWNER)
   __shared__ int is_last;
   __shared__ int q_cnt;  // candidates found (may exceed kCap: overflow)
-  __shared__ float w_max[kWarps];
-  __shared__ uint32_t w_mk[kWarps], w_tk[kWarps];
-  __shared__ double w_sum[kWarps];
-  __shared__ int w_bi[kWarps];
+  __shared__ float w_max[NW];
+  __shared__ uint32_t w_mk[NW], w_tk[NW];
+  __shared__ double w_sum[NW];
+  __shared__ int w_bi[NW];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int r = blockIdx.x, c = blockIdx.y;  // rows vary fastest in launch order
@@ -555,6 +677,12 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
   const float* g = A.logits + (int64_t)r * A.ld + c0;
   const bool bulk = ((reinterpret_cast<uintptr_t>(g) & 15) == 0) && ((n & 3) == 0);
   const bool stall = A.test_wait > 0 && r == 0 && c == 0;
+  // the row's history range, loaded now so the load overlaps the setup
+  int64_t h0 = 0, h1 = 0;
+  if (PEN) {
+    h0 = __ldg(A.hist_off + r);
+    h1 = __ldg(A.hist_off + r + 1);
+  }
 
   if (tid == 0) {
     if (bulk)
@@ -562,7 +690,9 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     if (stall) mbar_init(&stall_bar, 1);
     if (bulk || stall) fence_mbar_init();
   }
-  if (PEN) penmask[tid] = 0u;  // kChunk / 32 == kThreads words
+  if (PEN)
+#pragma unroll
+    for (int q = 0; q < kPenWords; q++) penmask[tid + q * NT] = 0u;
   if (tid == 0) q_cnt = 0;
   // whole-vocabulary rows: the chunk's mass histogram.  Counts (packed u16
   // pairs) only when a rank is selected (top_k above kKmax).  Masses in one
@@ -578,8 +708,8 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
   __shared__ int hwrap;
   if (tid == 0) hwrap = 0;
   if constexpr (MODE == kFull) {
-    for (int b = tid; b < kNB / 2 + kNB; b += kThreads) hcnt[b] = 0u;
-    for (int b = tid; b < kNB; b += kThreads) hscale[b] = nuc_scale(b);
+    for (int b = tid; b < kNB / 2 + kNB; b += NT) hcnt[b] = 0u;
+    for (int b = tid; b < kNB; b += NT) hscale[b] = nuc_scale(b);
   }
   __syncthreads();
   if (bulk) {
@@ -593,29 +723,12 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
       }
     }
   } else {
-    for (int j = tid; j < n; j += kThreads) tile[j] = __ldg(g + j);
+    for (int j = tid; j < n; j += NT) tile[j] = __ldg(g + j);
   }
-  for (int j = n + tid; j < kChunk; j += kThreads) tile[j] = -INFINITY;
+  for (int j = n + tid; j < kChunk; j += NT) tile[j] = -INFINITY;
 
   // ---- penalty bitmap of this chunk, built while the copies are in flight
-  if (PEN) {
-    const int64_t h0 = A.hist_off[r];
-    const int hn = (int)(A.hist_off[r + 1] - h0);
-    const int32_t* hrow = A.hist + h0;
-    for (int jb = 0; jb < hn; jb += 4 * kThreads) {
-      uint32_t ids[4];
-#pragma unroll
-      for (int q = 0; q < 4; q++) {
-        const int j = jb + q * kThreads + tid;
-        ids[q] = j < hn ? (uint32_t)__ldg(hrow + j) : 0xFFFFFFFFu;
-      }
-#pragma unroll
-      for (int q = 0; q < 4; q++) {
-        const uint32_t d = ids[q] - (uint32_t)(A.col0 + c0);  // ids outside the chunk wrap past n
-        if (d < (uint32_t)n) atomicOr(&penmask[d >> 5], 1u << (d & 31));
-      }
-    }
-  }
+  if (PEN) pen_scan<NT, true>(A, h0, h1, c0, n, penmask);
   // one thread waits for the copies; the rest park at the barrier
   int timed_out = 0;
   if (bulk && tid == 0) {
@@ -637,26 +750,33 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     __syncthreads();
   }
 
-  // ---- apply the penalty to the flagged logits (one bitmap word per thread)
+  // ---- the penalty, applied in shared memory by the thread that reads each
+  // flagged element in the streaming loops (its bits of the thread-major
+  // bitmap), so no barrier is needed before those loops
   if (PEN) {
-    uint32_t w = penmask[tid];
-    while (w) {
-      const int b = __ffs(w) - 1;
-      w &= w - 1;
-      const int j = tid * 32 + b;
-      tile[j] = pen_apply_fast(tile[j], A.pen, A.rpen);
+#pragma unroll
+    for (int q = 0; q < kPenWords; q++) {
+      uint32_t w = penmask[tid * kPenWords + q];
+      while (w) {
+        const int b = 32 * q + __ffs(w) - 1;  // bit 4 * step + lane of the float4
+        w &= w - 1;
+        const int j = 4 * (tid + (b >> 2) * NT) + (b & 3);
+        tile[j] = pen_apply_fast(tile[j], A.pen, A.rpen);
+      }
     }
-    __syncthreads();
-  }
-  // diagnostics: the penalised logits, the reference's `work` before the
-  // temperature divide (src/generation.js:72-75)
-  if (A.d_pen) {
-    float* dp = A.d_pen + (int64_t)r * A.pen_ld + c0;
-    for (int j = tid; j < n; j += kThreads) dp[j] = tile[j];
   }
 
+  // diagnostics: the penalised logits, the reference's `work` before the
+  // temperature divide (src/generation.js:72-75); called after a barrier that
+  // follows the first streaming loop
+  auto write_pen_diag = [&]() {
+    float* dp = A.d_pen + (int64_t)r * A.pen_ld + c0;
+    for (int j = tid; j < n; j += NT) dp[j] = tile[j];
+  };
+
   const float4* t4 = reinterpret_cast<const float4*>(tile);
-  constexpr int kIters = kChunk / 4 / kThreads;  // 8 float4 per thread
+  constexpr int kIters = kChunk / 4 / NT;  // float4 per thread
+  static_assert(kIters <= 32, "one candidate-mask bit per float4 of a thread");
 
   if (MODE == kGreedy) {
     // first index of the strict max (src/generation.js:51-55)
@@ -664,7 +784,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     int bi = INT_MAX;
 #pragma unroll 4
     for (int i = 0; i < kIters; i++) {
-      const int q = tid + i * kThreads;
+      const int q = tid + i * NT;
       const float4 v = t4[q];
       const int j = c0 + 4 * q;
       if (v.x > bv) { bv = v.x; bi = j; }
@@ -680,8 +800,9 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     }
     if (lane == 0) { w_max[warp] = bv; w_bi[warp] = bi; }
     __syncthreads();
+    if (A.d_pen) write_pen_diag();
     if (tid == 0) {
-      for (int w = 1; w < kWarps; w++)
+      for (int w = 1; w < NW; w++)
         if (w_max[w] > bv || (w_max[w] == bv && w_bi[w] < bi)) { bv = w_max[w]; bi = w_bi[w]; }
       ChunkStat st;
       st.m = bv; st.tau = bv; st.s = 0.0; st.n_cand = 0; st.best_i = bi; st.zref = 0.f; st.sig = bv;
@@ -692,18 +813,18 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     float tm = -INFINITY;
 #pragma unroll 4
     for (int i = 0; i < kIters; i++) {
-      const float4 v = t4[tid + i * kThreads];
+      const float4 v = t4[tid + i * NT];
       tm = fmax3(fmax3(tm, v.x, v.y), v.z, v.w);
     }
     // The warp's kw-th largest thread maximum, by kw rounds of a warp max
     // reduction over order-preserving keys, removing one instance per round.
     // At least kw thread maxima of every warp are >= it, so tau = min over
-    // warps is reached by >= kWarps*kw >= top_k distinct elements of the chunk.
-    // A partial chunk (n < 4 * kThreads) has data in its first w_act warps
-    // only, and takes a larger per-warp rank so those warps still cover keff.
+    // warps is reached by >= NW*kw >= top_k distinct elements of the chunk.
+    // A partial chunk (n < 4 * NT) has data in its first w_act warps only, and
+    // takes a larger per-warp rank so those warps still cover keff.
     const int keff = (MODE == kTopK) ? A.k : A.ksum;
-    const int w_act = min(kWarps, ((n + 3) / 4 + 31) / 32);
-    const int kwc = (n >= 4 * kThreads) ? A.kw : min(32, (keff + w_act - 1) / w_act);
+    const int w_act = (n >= 4 * NT) ? NW : min(NW, ((n + 3) / 4 + 31) / 32);
+    const int kwc = min(32, max(1, (keff + w_act - 1) / w_act));
     const uint32_t tkey = fkey(tm);  // tm is never NaN
     const uint32_t wmk = __reduce_max_sync(kAll, tkey);
     uint32_t kk = tkey, wtk = wmk;
@@ -714,14 +835,15 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     }
     if (lane == 0) { w_mk[warp] = wmk; w_tk[warp] = wtk; }
     __syncthreads();
-    const float m = fkey_inv(__reduce_max_sync(kAll, lane < kWarps ? w_mk[lane] : 0u));
+    if (A.d_pen) write_pen_diag();
+    const float m = fkey_inv(__reduce_max_sync(kAll, lane < NW ? w_mk[lane] : 0u));
     // Warps whose kwc-th thread maximum is -inf (padding past the row end, or
     // -inf logits) are left out of the minimum.  The minimum over the others
     // is the chunk's top-k bound tau when they alone hold keff elements
     // (kwc each); otherwise tau = -inf.  sig is the storage threshold: every
     // element >= sig becomes a candidate, and the finalizer falls back to the
     // exact rescan when some chunk's sig is above the row's tau.
-    const uint32_t wk = lane < kWarps ? w_tk[lane] : 0u;
+    const uint32_t wk = lane < NW ? w_tk[lane] : 0u;
     const bool wok = wk > fkey(-INFINITY);
     const int n_ok = __popc(__ballot_sync(kAll, wok));
     const float tmin = n_ok ? fkey_inv(__reduce_min_sync(kAll, wok ? wk : 0xFFFFFFFFu)) : -INFINITY;
@@ -762,7 +884,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
       const unsigned long long a2 = f2_pack(a, a), nz2 = f2_pack(-zref, -zref);
 #pragma unroll 4
       for (int i = 0; i < kIters; i++) {
-        const float4 v = t4[tid + i * kThreads];
+        const float4 v = t4[tid + i * NT];
         const float2 z01 = f2_unpack(f2_fma(f2_pack(v.x, v.y), a2, nz2));
         const float2 z23 = f2_unpack(f2_fma(f2_pack(v.z, v.w), a2, nz2));
         const unsigned long long e01 = f2_pack(ex2_approx(z01.x), ex2_approx(z01.y));
@@ -781,7 +903,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     } else {
       // partial chunk, or zref out of range: one element at a time
       for (int i = 0; i < kIters; i++) {
-        const int qq = tid + i * kThreads;
+        const int qq = tid + i * NT;
         const float4 v = t4[qq];
         const int j = 4 * qq;
         const float xs[4] = {v.x, v.y, v.z, v.w};
@@ -804,7 +926,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     while (cmask) {
       const int i = __ffs(cmask) - 1;
       cmask &= cmask - 1u;
-      const int qq = tid + i * kThreads;
+      const int qq = tid + i * NT;
       const float4 v = t4[qq];
       const int j = 4 * qq, gj = c0 + j;
       const bool k0 = v.x >= sig && j < n, k1 = v.y >= sig && j + 1 < n;
@@ -820,7 +942,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     if (lane == 0) w_sum[warp] = ds;
     __syncthreads();
     if (warp == 0) {
-      const double S = warp_sum(lane < kWarps ? w_sum[lane] : 0.0);
+      const double S = warp_sum(lane < NW ? w_sum[lane] : 0.0);
       if (lane == 0) {
         ChunkStat st;
         st.m = m; st.tau = tau; st.s = S; st.n_cand = min(q_cnt, kCap + 1);
@@ -832,7 +954,7 @@ __global__ void __launch_bounds__(kThreads, 3) sample_kernel(const __grid_consta
     }
     if constexpr (MODE == kFull) {
       const int64_t hb = ((int64_t)r * A.n_chunks + c) * kNB;
-      for (int b = tid; b < kNB; b += kThreads) {
+      for (int b = tid; b < kNB; b += NT) {
         if (hcounts) A.h_cnt[hb + b] = (uint16_t)((hcnt[b >> 1] >> ((b & 1) << 4)) & 0xFFFFu);
         A.h_mass[hb + b] = hwrap ? __longlong_as_double(0x7ff8000000000000ll) : (double)hq[b] / (double)hscale[b];
       }
@@ -1183,7 +1305,7 @@ namespace ms {
 
 static_assert(sizeof(FinSmem) <= kChunk * sizeof(float), "finalize scratch must fit in the chunk tile");
 static_assert(sizeof(FullSmem) <= kChunk * sizeof(float), "full-row scratch must fit in the chunk tile");
-static_assert(kChunk / 32 == kThreads, "one penalty bitmap word per thread");
+static_assert(kChunk / 32 % 256 == 0 && kChunk / 32 % kThreads == 0, "whole penalty bitmap words per thread");
 
 // =============================================================== launch
 namespace {
@@ -1239,7 +1361,7 @@ cudaError_t set_fin_attrs() {
 
 template <int MODE, bool PEN>
 cudaError_t launch_mode(const Args& S, dim3 grid, cudaStream_t stream, cudaEvent_t mid) {
-  sample_kernel<MODE, PEN><<<grid, dim3(kThreads), chunk_smem<MODE>(), stream>>>(S);
+  sample_kernel<MODE, PEN><<<grid, dim3(chunk_threads<MODE>()), chunk_smem<MODE>(), stream>>>(S);
   cudaError_t e = cudaGetLastError();
   if (mid) cudaEventRecord(mid, stream);
   if constexpr (MODE == kGreedy) {
@@ -1277,8 +1399,8 @@ constexpr size_t kShardSmem = sizeof(FinSmem);
 template <int MODE>
 cudaError_t launch_shard_mode(const Args& S, bool pen, cudaStream_t stream) {
   const dim3 grid(S.B, S.n_chunks);
-  if (pen) sample_kernel<MODE, true><<<grid, dim3(kThreads), kSmem, stream>>>(S);
-  else sample_kernel<MODE, false><<<grid, dim3(kThreads), kSmem, stream>>>(S);
+  if (pen) sample_kernel<MODE, true><<<grid, dim3(chunk_threads<MODE>()), kSmem, stream>>>(S);
+  else sample_kernel<MODE, false><<<grid, dim3(chunk_threads<MODE>()), kSmem, stream>>>(S);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};

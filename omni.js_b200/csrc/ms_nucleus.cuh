@@ -332,13 +332,7 @@ __global__ void __launch_bounds__(kThreads, 3) nucleus_extract_kernel(const __gr
     for (int j = tid; j < n; j += kThreads) tile[j] = __ldg(g + j);
   }
   for (int j = n + tid; j < kChunk; j += kThreads) tile[j] = __int_as_float(0x7fc00000);  // padding fails every test
-  if (PEN) {  // the chunk's penalty bitmap while the copies fly
-    const int64_t h0 = A.hist_off[r], h1 = A.hist_off[r + 1];
-    for (int64_t h = h0 + tid; h < h1; h += kThreads) {
-      const uint32_t d = (uint32_t)__ldg(A.hist + h) - (uint32_t)c0;  // ids outside wrap past n
-      if (d < (uint32_t)n) atomicOr(&penmask[d >> 5], 1u << (d & 31));
-    }
-  }
+  if (PEN) pen_bitmap<kThreads>(A, r, c0, n, penmask);  // the chunk's penalty bitmap while the copies fly
   int timed_out = 0;
   if (bulk && tid == 0)
     for (int s = 0; s < kSub; s++)
