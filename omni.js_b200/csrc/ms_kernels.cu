@@ -346,7 +346,10 @@ __device__ void row_stats(const Args& A, int r, FinSmem& F) {
   } else if (warp == 1) {
     if (lane == 0) F.u = A.u ? __ldg(A.u + r) : 0.0;
     for (int b = lane; b < 256; b += 32) { F.h1[b] = 0; F.h2[b] = 0; }
-    if (lane == 0) { F.n_top = 0; F.n_bkt = 0; }
+    if (lane == 0) { F.n_top = 0; F.n_bkt = 0; F.n_keep = 0; F.kx = 0u; }
+  } else {  // the other warps clear narrow_terms' histograms
+    int* wh = reinterpret_cast<int*>(F.keys);
+    for (int b = tid - 64; b < 8 * 256; b += (int)blockDim.x - 64) wh[b] = 0;
   }
   __syncthreads();
 }
@@ -386,38 +389,52 @@ __device__ void gather_cands(const Args& A, int r, FinSmem& F) {
   __syncthreads();
 }
 
-// Narrows the nfc gathered candidates (all x >= tau_row, M the row max) to
-// those that can still be among the top k: a 256-bin histogram of x over
-// [tau_row, M] (per-warp copies in F.keys, so few lanes meet on one counter)
-// finds the bin holding the k-th largest x; the candidates of that bin and the
-// bins above it move to the front of F.gath.  Returns the new count, or nfc
-// when nothing is narrowed, and sets *xout to the largest x left out (-inf:
-// none).  F.h1, F.h2, F.n_top, F.n_bkt are zero again on return.  Ends with a
-// barrier.
-__device__ int narrow_cands(FinSmem& F, int nfc, int k, float tau_row, float M, float* xout) {
-  const int tid = threadIdx.x, warp = tid >> 5, nt = (int)blockDim.x;
+// The exact softmax term of a gathered candidate (src/generation.js:14) and
+// its correction of the fast sum (exact minus fast term, in 2^-50 units).
+__device__ __forceinline__ float cand_term(const Args& A, const FinSmem& F, const ChunkStat* st, const Cand& cd,
+                                           float Mp, long long* corr) {
+  const int c = cd.i / kChunk;
+  const float mc = c < kFinChunks ? F.cm[c] : __ldcg(&st[c].m);
+  const float zc = c < kFinChunks ? F.cz[c] : __ldcg(&st[c].zref);
+  const double sc = c < kFinChunks ? F.cs[c] : chunk_scale(A, mc, zc, Mp);
+  const float e = term_exact(temper_fast(cd.x, A.T, A.rT, A.temper), Mp);
+  *corr += __double2ll_rn(((double)e - (double)chunk_term(A, cd.x, mc, zc) * sc) * 1125899906842624.0);
+  return e;
+}
+
+// Top-k rows: narrows the nfc gathered candidates (all x >= tau_row, M the row
+// max) to those that can still be among the top k.  A 256-bin histogram of x
+// over [tau_row, M] (per-warp copies in F.keys, cleared by row_stats, so few
+// lanes meet on one counter) finds the bin of the k-th largest x; the
+// candidates of that bin and the bins above it go to F.top as Cand, then get
+// their exact terms in x (one per thread) and their corrections in F.corr.
+// Returns their number (>= k), with *xout the largest x left out (-inf:
+// none), or -1 when nothing is narrowed (F.corr, F.h1 and F.h2 are then as
+// row_stats left them).  Ends with a barrier.
+__device__ int narrow_terms(const Args& A, FinSmem& F, const ChunkStat* st, int nfc, float tau_row, float M,
+                            float Mp, float* xout) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nt = (int)blockDim.x;
+  const int k = A.k;
   *xout = -INFINITY;
   const float span = M - tau_row;
   // nothing to gain, or no finite range to bin over (uniform across the CTA)
-  if (nfc <= 2 * k || !(span > 0.f) || !(span <= FLT_MAX)) return nfc;
+  if (nfc <= 2 * k || !(span > 0.f) || !(span <= FLT_MAX)) return -1;
   const float inv_w = 256.f / span;
   auto bin = [&](float x) { return min(255, max(0, __float2int_rd(__fmul_rn(__fsub_rn(x, tau_row), inv_w)))); };
   int* wh = reinterpret_cast<int*>(F.keys);  // 8 histograms of 256 bins
-  for (int b = tid; b < 8 * 256; b += nt) wh[b] = 0;
-  if (tid == 0) { F.n_keep = 0; F.kx = 0u; }
-  __syncthreads();
   int* myh = wh + (warp & 7) * 256;
   for (int j = tid; j < nfc; j += nt) atomicAdd(&myh[bin(F.gath[j].x)], 1);
   __syncthreads();
-  // bins in descending x: F.h1[255 - b] counts bin b
-  for (int b = tid; b < 256; b += nt) {
-    int t = 0;
+  if (warp == 0) {  // bins in descending x: F.h1[255 - b] counts bin b
+    for (int b = lane; b < 256; b += 32) {
+      int t = 0;
 #pragma unroll
-    for (int w = 0; w < 8; w++) t += wh[w * 256 + b];
-    F.h1[255 - b] = t;
+      for (int w = 0; w < 8; w++) t += wh[w * 256 + b];
+      F.h1[255 - b] = t;
+    }
+    __syncwarp();
+    scan_pick(F.h1, k, &F.b1, &F.need);
   }
-  __syncthreads();
-  if (warp == 0) scan_pick(F.h1, k, &F.b1, &F.need);
   __syncthreads();
   const int bk = 255 - F.b1;  // the bin of the k-th largest x: keep bins >= bk
   Cand* keep = reinterpret_cast<Cand*>(F.top);  // room for kKmax candidates
@@ -432,16 +449,57 @@ __device__ int narrow_cands(FinSmem& F, int nfc, int k, float tau_row, float M, 
   }
   __syncthreads();
   const int nk = F.n_keep;
-  const uint32_t kx = F.kx;
-  if (nk <= kKmax) {
-    for (int j = tid; j < nk; j += nt) F.gath[j] = keep[j];
+  if (nk > kKmax) {  // too many in the bin: leave F.h1 as it was
+    for (int b = tid; b < 256; b += nt) F.h1[b] = 0;
+    __syncthreads();
+    return -1;
   }
-  for (int b = tid; b < 256; b += nt) { F.h1[b] = 0; F.h2[b] = 0; }
-  if (tid == 0) { F.n_top = 0; F.n_bkt = 0; }
+  // the exact terms, one candidate per thread
+  long long corr = 0;
+  for (int j = tid; j < nk; j += nt) keep[j].x = cand_term(A, F, st, keep[j], Mp, &corr);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) corr += __shfl_xor_sync(kAll, corr, o);
+  if (lane == 0 && corr != 0) atomicAdd(&F.corr, (unsigned long long)corr);
   __syncthreads();
-  if (nk > kKmax) return nfc;
-  *xout = kx ? fkey_inv(kx) : -INFINITY;
+  *xout = F.kx ? fkey_inv(F.kx) : -INFINITY;
   return nk;
+}
+
+// topk_from_terms for the n (k <= n <= kKmax) narrowed candidates in F.top:
+// every key is ranked against all others in one pass.  Same contract
+// otherwise (F.pout read after the first barrier; false: cannot settle).
+__device__ bool topk_small(const Args& A, int r, FinSmem& F, int n, double S, double rS, float Mp) {
+  const int tid = threadIdx.x, warp = tid >> 5, nt = (int)blockDim.x;
+  const int k = A.k;
+  const Cand* cands = reinterpret_cast<const Cand*>(F.top);
+  unsigned long long* key = F.keys;
+  for (int j = tid; j < n; j += nt) {
+    const Cand cd = cands[j];
+    const float p = div_to_f32((double)cd.x, S, rS);
+    key[j] = ((unsigned long long)(0xFFFFFFFFu - __float_as_uint(p)) << 32) | (uint32_t)cd.i;
+  }
+  __syncthreads();
+  unsigned long long* sorted = F.top;  // the candidates are no longer read
+  for (int t = tid; t < n; t += nt) {  // keys are distinct: the ids differ
+    const unsigned long long kk = key[t];
+    int rank = 0;
+    for (int j = 0; j < n; j++) rank += key[j] < kk;
+    if (rank < k) sorted[rank] = kk;
+  }
+  __syncthreads();
+  if (!(F.pout < (float)key_prob(sorted[k - 1]))) return false;
+  if (warp == 0) topk_draw(A, r, sorted, Mp, S, F.u, &F.nF);
+  __syncthreads();
+  if (A.d_cand_ids || A.d_cand_probs) {
+    const int nn = F.nF;  // set by topk_draw
+    for (int i = tid; i < nn && i < A.cand_cap; i += nt) {
+      const unsigned long long kkey = sorted[i];
+      if (A.d_cand_ids) A.d_cand_ids[(int64_t)r * A.cand_cap + i] = (int32_t)(uint32_t)kkey;
+      if (A.d_cand_probs)
+        A.d_cand_probs[(int64_t)r * A.cand_cap + i] = __uint_as_float(0xFFFFFFFFu - (uint32_t)(kkey >> 32));
+    }
+  }
+  return true;
 }
 
 template <int MODE>
@@ -504,31 +562,28 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
   if (nf > kGathMax || (MODE == kTopK && nf < A.k)) {
     if (tid == 0) F.slow = 1;
   }
-  // ---- top-k rows: only the candidates that can reach the top k go on (the
-  // largest x left out bounds every probability outside them)
+  // ---- top-k rows: only the candidates that can reach the top k go on, with
+  // their exact terms (the largest x left out bounds every probability
+  // outside them)
   float xout = -INFINITY;
-  if (MODE == kTopK && nf <= kGathMax && nf >= A.k) nfc = narrow_cands(F, nfc, A.k, tau_row, M, &xout);
+  int nk = -1;
+  if (MODE == kTopK && !F.slow && nf <= kGathMax && nf >= A.k) nk = narrow_terms(A, F, st, nfc, tau_row, M, Mp, &xout);
 
-  // ---- exact terms of every remaining candidate (kept in place of x) and the
-  // fast sum's correction: exact minus fast term, summed in 2^-50 units
-  {
+  // ---- otherwise the exact terms of every gathered candidate (kept in place
+  // of x) and the fast sum's correction: exact minus fast term, summed in
+  // 2^-50 units
+  if (nk < 0) {
     long long corr = 0;
     for (int j = tid; j < nfc; j += nt) {
       Cand cd = F.gath[j];
-      const int c = cd.i / kChunk;
-      const float mc = c < kFinChunks ? F.cm[c] : __ldcg(&st[c].m);
-      const float zc = c < kFinChunks ? F.cz[c] : __ldcg(&st[c].zref);
-      const double sc = c < kFinChunks ? F.cs[c] : chunk_scale(A, mc, zc, Mp);
-      const float e = term_exact(temper_fast(cd.x, A.T, A.rT, A.temper), Mp);
-      corr += __double2ll_rn(((double)e - (double)chunk_term(A, cd.x, mc, zc) * sc) * 1125899906842624.0);
-      cd.x = e;
+      cd.x = cand_term(A, F, st, cd, Mp, &corr);
       F.gath[j] = cd;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) corr += __shfl_xor_sync(kAll, corr, o);
     if (lane == 0 && corr != 0) atomicAdd(&F.corr, (unsigned long long)corr);
+    __syncthreads();
   }
-  __syncthreads();
   const double S = F.S_fast + (double)(long long)F.corr * (1.0 / 1125899906842624.0);
 
   RowInfo R;
@@ -561,7 +616,7 @@ __device__ __forceinline__ void finalize_row(const Args& A, int r, FinSmem& F) {
       }
       F.pout = po;
     }
-    if (topk_from_terms(A, r, F, nfc, S, rS, Mp)) return;
+    if (nk >= 0 ? topk_small(A, r, F, nk, S, rS, Mp) : topk_from_terms(A, r, F, nfc, S, rS, Mp)) return;
   }
   // ---- exact rescan of the whole row
   const int flags = (MODE == kTopK) ? MS_ROW_SLOWPATH : 0;
