@@ -57,6 +57,9 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-verify", action="store_true")
     ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--rows", type=int, default=0,
+                    help="one GPU: sample only the first ROWS rows of the batch (a smaller case of the same "
+                         "kernels, for profiling captures); the line's config says so")
     return ap.parse_args()
 
 
@@ -418,6 +421,8 @@ def run_ours(args, rank, world, local_rank):
     else:
         r0, r1 = row_shard(w.B, world, rank)
         b_rank = r1 - r0
+    if args.rows > 0 and world == 1:
+        b_rank = min(b_rank, args.rows)
     seed = args.seed + 7919 * rank
     clocks = ClockSampler(local_rank)
     r = time_rows(args, w, b_rank, seed, dev, world, local_rank, sampler, clocks=clocks,
@@ -447,6 +452,8 @@ def run_ours(args, rank, world, local_rank):
     achieved = bytes_launch / (r["chunk_ms"] / 1e3) / 1e9 if r["chunk_ms"] > 0 else 0.0
     scaling = "weak" if args.weak else "strong"
     gb = w.B * world if args.weak else w.B
+    if args.rows > 0 and world == 1:
+        gb = b_rank
     line = {
         "metric": "sampled rows/sec at batch x vocab",
         "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
