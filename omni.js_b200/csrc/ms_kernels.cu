@@ -754,14 +754,14 @@ __global__ void __launch_bounds__(chunk_threads<MODE>(), 3) sample_kernel(const 
   // 32-bit word per bin, scaled per bin: an element of local bin b has a fast
   // term e within 2^(+-1/16) of 2^(-b/16), so q = e * hscale[b] with
   // hscale[b] = 2^(21 + b/16) is below 2^21.1, rounded to within 2^-22 of
-  // its value (one atomic per element, no carry word).  A bin of more than
-  // about 1900 elements can wrap the word: the chunk then marks its histogram
-  // invalid (mass NaN) and the row takes the exact whole-row path.
+  // its value (one atomic per element, no carry word).  A bin of kWrapCount
+  // elements or more may have wrapped its word: its mass is written as NaN
+  // and the row takes the exact whole-row path.  Both adds are fire and
+  // forget: nothing waits for their results.
   uint32_t* hcnt = reinterpret_cast<uint32_t*>(dyn_smem + kChunk * sizeof(float));
   uint32_t* hq = hcnt + kNB / 2;
   float* hscale = reinterpret_cast<float*>(hq + kNB);
-  __shared__ int hwrap;
-  if (tid == 0) hwrap = 0;
+  constexpr uint32_t kWrapCount = 1900;  // below 2^32 / 2^21.0625, the bound on q
   if constexpr (MODE == kFull) {
     for (int b = tid; b < kNB / 2 + kNB; b += NT) hcnt[b] = 0u;
     for (int b = tid; b < kNB; b += NT) hscale[b] = nuc_scale(b);
@@ -923,10 +923,8 @@ __global__ void __launch_bounds__(chunk_threads<MODE>(), 3) sample_kernel(const 
     auto hist_add = [&](float x, float e) {
       if (x != x) return;  // a NaN makes the whole row NaN
       const int lb = nuc_local(nuc_bin(x, a16), btop);
-      if (hcounts) atomicAdd(&hcnt[lb >> 1], 1u << ((lb & 1) << 4));
-      const uint32_t q = __float2uint_rn(__fmul_rn(e, hscale[lb]));
-      const uint32_t old = atomicAdd(&hq[lb], q);
-      if (old + q < old) hwrap = 1;
+      atomicAdd(&hcnt[lb >> 1], 1u << ((lb & 1) << 4));  // u16 pairs: a chunk holds < 2^16
+      atomicAdd(&hq[lb], __float2uint_rn(__fmul_rn(e, hscale[lb])));
     };
     auto kahan = [&](float t) {
       const float y = __fsub_rn(t, comp);
@@ -1010,8 +1008,10 @@ __global__ void __launch_bounds__(chunk_threads<MODE>(), 3) sample_kernel(const 
     if constexpr (MODE == kFull) {
       const int64_t hb = ((int64_t)r * A.n_chunks + c) * kNB;
       for (int b = tid; b < kNB; b += NT) {
-        if (hcounts) A.h_cnt[hb + b] = (uint16_t)((hcnt[b >> 1] >> ((b & 1) << 4)) & 0xFFFFu);
-        A.h_mass[hb + b] = hwrap ? __longlong_as_double(0x7ff8000000000000ll) : (double)hq[b] / (double)hscale[b];
+        const uint32_t cnt = (hcnt[b >> 1] >> ((b & 1) << 4)) & 0xFFFFu;
+        if (hcounts) A.h_cnt[hb + b] = (uint16_t)cnt;
+        A.h_mass[hb + b] = cnt >= kWrapCount ? __longlong_as_double(0x7ff8000000000000ll)
+                                             : (double)hq[b] / (double)hscale[b];
       }
     }
   }
