@@ -361,20 +361,28 @@ __device__ void gather_cands(const Args& A, int r, FinSmem& F) {
   const int nw = (int)(blockDim.x >> 5);
   const ChunkStat* st = A.stats + (int64_t)r * A.n_chunks;
   const float tau_row = F.tau_row;
-  for (int c = warp; c < A.n_chunks; c += nw) {  // one chunk per warp at a time
-    const int nc = min(__ldcg(&st[c].n_cand), kCap);
-    const Cand* src = A.cands + ((int64_t)r * A.n_chunks + c) * kCap;
-    for (int j0 = 0; j0 < nc; j0 += 128) {
-      float2 v[4];
+  // two chunks per warp at a time (c and c + nw): both list lengths, then
+  // eight entries per lane, are in flight together
+  for (int c = warp; c < A.n_chunks; c += 2 * nw) {
+    const int c2 = c + nw;
+    const bool two = c2 < A.n_chunks;
+    const int nc0 = min(__ldcg(&st[c].n_cand), kCap);
+    const int nc1 = two ? min(__ldcg(&st[c2].n_cand), kCap) : 0;
+    const Cand* src0 = A.cands + ((int64_t)r * A.n_chunks + c) * kCap;
+    const Cand* src1 = A.cands + ((int64_t)r * A.n_chunks + (two ? c2 : c)) * kCap;
+    for (int j0 = 0; j0 < max(nc0, nc1); j0 += 128) {
+      float2 v[8];
 #pragma unroll
-      for (int t = 0; t < 4; t++) {  // four loads in flight per lane
-        const int j = j0 + 32 * t + lane;
+      for (int t = 0; t < 8; t++) {
+        const int j = j0 + 32 * (t & 3) + lane;
+        const int nc = t < 4 ? nc0 : nc1;
+        const Cand* src = t < 4 ? src0 : src1;
         v[t] = j < nc ? __ldcg(reinterpret_cast<const float2*>(src + j)) : make_float2(-INFINITY, 0.f);
       }
 #pragma unroll
-      for (int t = 0; t < 4; t++) {
-        const int j = j0 + 32 * t + lane;
-        const bool keep = j < nc && v[t].x >= tau_row;
+      for (int t = 0; t < 8; t++) {
+        const int j = j0 + 32 * (t & 3) + lane;
+        const bool keep = j < (t < 4 ? nc0 : nc1) && v[t].x >= tau_row;
         const unsigned msk = __ballot_sync(kAll, keep);
         if (msk) {
           int base = 0;
