@@ -164,10 +164,10 @@ int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V, int64_t ld
  * Kernel time of the calls made with MS_PROFILE since the last read, summed
  * over calls (milliseconds, CUDA events on the launch stream):
  *   stream_ms    the chunk kernel, which reads every logit once
- *   finalize_ms  the per-row finalize kernel; 0 when the chunk kernel's last
- *                CTA of each row finalizes it (greedy rows, or
- *                MS_SPLIT_FINALIZE=0 in the environment), whose time is then
- *                part of stream_ms
+ *   finalize_ms  the kernels after it: the per-row finalize (top-k rows), or
+ *                the plan, extract and resolve kernels (whole-vocabulary
+ *                rows); 0 for greedy rows, whose chunk kernel's last CTA of
+ *                each row finalizes it (its time is then part of stream_ms)
  * In a profiled call an event sits between the two kernels, so the finalize
  * cannot start early; profile a sample of the calls, not all of them.
  * Waits for those calls' events.  No reference counterpart: the reference
@@ -177,10 +177,11 @@ int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V, int64_t ld
 int ms_profile_read(ms_ctx* ctx, double* stream_ms, double* finalize_ms, int64_t* calls);
 
 /*
- * Kernels this context has launched (all its devices, since ms_create): one
- * per ms_sample call when greedy, two when sampled (the chunk kernel and the
- * row finalize), per slice of rows (a slice holds about 2^31 / ceil(V/16384)
- * rows).  No reference counterpart.
+ * Kernels this context has launched (all its devices, since ms_create): per
+ * ms_sample call and slice of rows (a slice holds about 2^31 / ceil(V/16384)
+ * rows), one when greedy, two for top-k rows (the chunk kernel and the row
+ * finalize), four for whole-vocabulary rows (chunk kernel, plan, extract,
+ * resolve); one per ms_history_append.  No reference counterpart.
  */
 int ms_launch_count(ms_ctx* ctx, int64_t* kernels);
 
