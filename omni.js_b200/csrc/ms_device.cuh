@@ -54,6 +54,8 @@ struct ChunkStat {
   float sig;      // storage threshold: every element >= sig is among the candidates (sig >= tau)
 };
 
+static_assert(sizeof(ChunkStat) == 32, "chunk stats: two 16-byte loads");
+
 struct Cand {
   float x;        // penalised (untempered) logit
   int32_t i;      // vocabulary id

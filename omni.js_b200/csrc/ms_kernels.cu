@@ -303,16 +303,27 @@ __device__ void row_stats(const Args& A, int r, FinSmem& F) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const ChunkStat* st = A.stats + (int64_t)r * A.n_chunks;
   if (warp == 0) {
+    // a chunk's stats in two 16-byte loads (the array is 32-byte aligned); the
+    // lane's first chunk is kept for the second loop
+    auto load_stat = [&](int c) {
+      ChunkStat v;
+      const int4* p = reinterpret_cast<const int4*>(st + c);
+      int4* q = reinterpret_cast<int4*>(&v);
+      q[0] = __ldcg(p);
+      q[1] = __ldcg(p + 1);
+      return v;
+    };
+    ChunkStat first;
     float M = -INFINITY, tr = -INFINITY, sg = -INFINITY;
     int nanr = 0, ovf = 0;
     for (int c = lane; c < A.n_chunks; c += 32) {
-      const float m = __ldcg(&st[c].m), t = __ldcg(&st[c].tau);
-      const double s = __ldcg(&st[c].s);
-      M = fmaxf(M, m);
-      tr = fmaxf(tr, t);
-      sg = fmaxf(sg, __ldcg(&st[c].sig));
-      nanr |= (s != s);
-      ovf |= (__ldcg(&st[c].n_cand) > kCap);
+      const ChunkStat v = load_stat(c);
+      if (c == lane) first = v;
+      M = fmaxf(M, v.m);
+      tr = fmaxf(tr, v.tau);
+      sg = fmaxf(sg, v.sig);
+      nanr |= (v.s != v.s);
+      ovf |= (v.n_cand > kCap);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -330,10 +341,10 @@ __device__ void row_stats(const Args& A, int r, FinSmem& F) {
     double S = 0.0;
     if (!nanr) {
       for (int c = lane; c < A.n_chunks; c += 32) {
-        const float m = __ldcg(&st[c].m), z = __ldcg(&st[c].zref);
-        const double sc = chunk_scale(A, m, z, Mp);
-        if (m != -INFINITY) S += __ldcg(&st[c].s) * sc;
-        if (c < kFinChunks) { F.cm[c] = m; F.cz[c] = z; F.cs[c] = sc; }
+        const ChunkStat v = (c == lane) ? first : load_stat(c);
+        const double sc = chunk_scale(A, v.m, v.zref, Mp);
+        if (v.m != -INFINITY) S += v.s * sc;
+        if (c < kFinChunks) { F.cm[c] = v.m; F.cz[c] = v.zref; F.cs[c] = sc; }
       }
       S = warp_sum(S);
     }
