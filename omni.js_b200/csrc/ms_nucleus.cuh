@@ -449,13 +449,15 @@ struct ResSmem {
 };
 constexpr double kTwo60 = 1152921504606846976.0;
 
-__device__ __forceinline__ void add_mass60(uint32_t* lo, uint32_t* hi, double mass) {
-  const unsigned long long u = (unsigned long long)(mass * kTwo60);
+// A mass in units of 2^-60 (truncated), added to a two-word shared counter.
+__device__ __forceinline__ unsigned long long mass60(double mass) { return (unsigned long long)(mass * kTwo60); }
+__device__ __forceinline__ void add_u60(uint32_t* lo, uint32_t* hi, unsigned long long u) {
   const uint32_t l = (uint32_t)u, h = (uint32_t)(u >> 32);
   const uint32_t old = atomicAdd(lo, l);
   const uint32_t up = h + ((old + l < old) ? 1u : 0u);
   if (up) atomicAdd(hi, up);
 }
+__device__ __forceinline__ void add_mass60(uint32_t* lo, uint32_t* hi, double mass) { add_u60(lo, hi, mass60(mass)); }
 
 // In one extracted range (m elements; cnt_above / mass_above the elements and
 // fast probability mass of the row above it), the first element in
@@ -541,12 +543,16 @@ __device__ bool select_in_list(const Args& A, const RowInfo& Ri, const Cand* L, 
   const float tl = R.tl, th = R.th;
   const float a16 = __fmul_rn(A.a, 16.f);
   if (!(__fmul_rn(-th, a16) >= wlo) || !(__fmul_rn(-tl, a16) < whi)) return false;
+  // the elements above the tie groups: their count and fast mass, summed per
+  // thread and per warp (the integer sum is the same in any order), one shared
+  // add per warp
   long long gc = 0;
+  unsigned long long gm = 0;
   for (int j = tid; j < m; j += nt) {
     const Cand cd = load(j);
     if (cd.x > th) {
       gc++;
-      add_mass60(&R.gt_lo, &R.gt_hi, mass_fast(Ri, cd.x));
+      gm += mass60(mass_fast(Ri, cd.x));
     } else if (cd.x >= tl) {
       const int q = atomicAdd(&R.n_key, 1);
       if (q < kExtCap)
@@ -554,8 +560,12 @@ __device__ bool select_in_list(const Args& A, const RowInfo& Ri, const Cand* L, 
     }
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) gc += __shfl_xor_sync(kAll, gc, o);
+  for (int o = 16; o > 0; o >>= 1) {
+    gc += __shfl_xor_sync(kAll, gc, o);
+    gm += __shfl_xor_sync(kAll, gm, o);
+  }
   if ((tid & 31) == 0 && gc) atomicAdd(reinterpret_cast<unsigned long long*>(&R.gt_c), (unsigned long long)gc);
+  if ((tid & 31) == 0 && gm) add_u60(&R.gt_lo, &R.gt_hi, gm);
   __syncthreads();
   const int nk = R.n_key;
   if (nk > kExtCap) return false;
