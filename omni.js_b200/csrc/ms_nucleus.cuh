@@ -35,6 +35,7 @@ struct NucSmem {
   long long red_c[32];
   double red_d[32];
   int red_i[32];
+  int ctop[kFinChunks];  // the chunks' top bins (first kFinChunks chunks)
 };
 
 // Inclusive block scan of one value per thread (blockDim.x == kNB).
@@ -146,8 +147,11 @@ __global__ void __launch_bounds__(kNB, 2) nucleus_plan_kernel(const __grid_const
 
   // ---- the row's top bin, then the chunk histograms on the row's bins
   int bmin = INT_MAX;
-  for (int c = tid; c < A.n_chunks; c += nt)
-    if (__ldcg(&st[c].m) != -INFINITY) bmin = min(bmin, __ldcg(&st[c].best_i));
+  for (int c = tid; c < A.n_chunks; c += nt) {
+    const int bi = __ldcg(&st[c].best_i);
+    if (c < kFinChunks) N.ctop[c] = bi;
+    if (__ldcg(&st[c].m) != -INFINITY) bmin = min(bmin, bi);
+  }
   bmin = __reduce_min_sync(kAll, bmin);
   if (lane == 0) N.red_i[tid >> 5] = bmin;
   __syncthreads();
@@ -157,6 +161,9 @@ __global__ void __launch_bounds__(kNB, 2) nucleus_plan_kernel(const __grid_const
   long long cnt = 0, tcnt = 0;
   double mass = 0.0, tmass = 0.0;
   const int t = tid;  // this thread's row bin, and the chunk bin it moves to the tail
+  // chunk tops come from shared memory, so the loads of several chunks'
+  // histogram words can be in flight at once
+#pragma unroll 4
   for (int c = 0; c < A.n_chunks; c++) {
     const float mc = c < kFinChunks ? F.cm[c] : __ldcg(&st[c].m);
     const int64_t hb = ((int64_t)r * A.n_chunks + c) * kNB;
@@ -166,7 +173,7 @@ __global__ void __launch_bounds__(kNB, 2) nucleus_plan_kernel(const __grid_const
     }
     const float zc = c < kFinChunks ? F.cz[c] : __ldcg(&st[c].zref);
     const double sc = (c < kFinChunks ? F.cs[c] : chunk_scale(A, mc, zc, Mp)) * rS;
-    const long long shift = (long long)__ldcg(&st[c].best_i) - (long long)b_row;
+    const long long shift = (long long)(c < kFinChunks ? N.ctop[c] : __ldcg(&st[c].best_i)) - (long long)b_row;
     const long long lb = (long long)t - shift;
     if (t < kNB - 1 && lb >= 0 && lb < kNB - 1) {
       if (counts) cnt += __ldcg(A.h_cnt + hb + lb);
