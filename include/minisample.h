@@ -27,7 +27,10 @@
  *     ordering them) race on that scratch.  Order such calls on one stream, or
  *     give each stream its own context.
  *   - Every bounded kernel wait that runs out marks its call as failed: the
- *     rows of that call get id -1 (and MS_ROW_TIMEOUT in diag->row_flags).  A
+ *     rows of that call get id -1 (and MS_ROW_TIMEOUT in diag->row_flags).
+ *     Top-k calls of at most 16 rows finalize each row as soon as its chunks
+ *     are done, so there only the rows finalized after the wait ran out get
+ *     -1 (always the row whose wait it was); the others keep correct ids.  A
  *     synchronous call (MS_HOST_PTRS, or MS_DEVICE_PTRS | MS_SYNC) then returns
  *     MS_ERR_TIMEOUT; an asynchronous device call reports it only through
  *     those -1 ids.  A later call is not affected.
@@ -166,8 +169,9 @@ int ms_sample(ms_ctx* ctx, const float* logits, int64_t B, int64_t V, int64_t ld
  *   stream_ms    the chunk kernel, which reads every logit once
  *   finalize_ms  the kernels after it: the per-row finalize (top-k rows), or
  *                the plan, extract and resolve kernels (whole-vocabulary
- *                rows); 0 for greedy rows, whose chunk kernel's last CTA of
- *                each row finalizes it (its time is then part of stream_ms)
+ *                rows); 0 for greedy rows and top-k calls of at most 16 rows,
+ *                whose chunk kernel's last CTA of each row finalizes it (its
+ *                time is then part of stream_ms)
  * In a profiled call an event sits between the two kernels, so the finalize
  * cannot start early; profile a sample of the calls, not all of them.
  * Waits for those calls' events.  No reference counterpart: the reference
@@ -179,8 +183,9 @@ int ms_profile_read(ms_ctx* ctx, double* stream_ms, double* finalize_ms, int64_t
 /*
  * Kernels this context has launched (all its devices, since ms_create): per
  * ms_sample call and slice of rows (a slice holds about 2^31 / ceil(V/16384)
- * rows), one when greedy, two for top-k rows (the chunk kernel and the row
- * finalize), four for whole-vocabulary rows (chunk kernel, plan, extract,
+ * rows), one when greedy or for top-k calls of at most 16 rows, two for
+ * larger top-k calls (the chunk kernel and the row finalize), four for
+ * whole-vocabulary rows (chunk kernel, plan, extract,
  * resolve); one per ms_history_append.  No reference counterpart.
  */
 int ms_launch_count(ms_ctx* ctx, int64_t* kernels);

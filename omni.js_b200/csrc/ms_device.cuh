@@ -117,6 +117,8 @@ struct Args {
   int32_t* list_cnt;     // [B, 4]: elements in each range, elements above each range
   int32_t* status;       // device status word (see above)
   int32_t epoch;         // this call's epoch (> 0)
+  int32_t fuse_fin;      // top-k rows: the chunk kernel's last CTA of each row finalizes it
+                         // (small batches: no second launch)
   long long test_wait;   // > 0: the first chunk CTA waits this many cycles on an
                          // mbarrier nothing completes (ms_debug_inject)
   float* d_pen;          // diagnostics: penalised logits [B, pen_ld] (may be null)

@@ -44,6 +44,7 @@ namespace ms {
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s: bound on every wait
 constexpr unsigned kAll = 0xffffffffu;
 constexpr int kFinChunks = 256;  // chunks whose scale the finalizer caches
+constexpr int kFuseRows = 16;    // top-k calls of at most this many rows finalize in the chunk kernel
 
 // =============================================================== shared scratch
 // =============================================================== finalize
@@ -728,7 +729,9 @@ __device__ __forceinline__ void pen_bitmap(const Args& A, int r, int c0, int n, 
 template <int MODE>
 __host__ __device__ constexpr int chunk_threads() { return MODE == kGreedy ? kThreads : 256; }
 
-template <int MODE, bool PEN>
+// FIN (top-k rows of small batches only): the last CTA of each row finalizes
+// it here, as greedy rows do, instead of a second grid.
+template <int MODE, bool PEN, bool FIN = false>
 __global__ void __launch_bounds__(chunk_threads<MODE>(), 3) sample_kernel(const __grid_constant__ Args A) {
   constexpr int NT = chunk_threads<MODE>(), NW = NT / 32;
   constexpr int kPenWords = kChunk / 32 / NT;  // penalty bitmap words per thread
@@ -1037,7 +1040,7 @@ __global__ void __launch_bounds__(chunk_threads<MODE>(), 3) sample_kernel(const 
 
   // ---- the last chunk of the row to finish finalizes it (unless a separate
   // finalize kernel follows)
-  if (MODE != kGreedy) {
+  if (MODE != kGreedy && !FIN) {
     // sampled rows: finalize_kernel follows; let it launch while the last
     // chunks stream
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -1054,7 +1057,7 @@ __global__ void __launch_bounds__(chunk_threads<MODE>(), 3) sample_kernel(const 
   if (is_last) {
     __threadfence();
     if (*((volatile int32_t*)A.status) != A.epoch) {
-      finalize_row<kGreedy>(A, r, *reinterpret_cast<FinSmem*>(dyn_smem));
+      finalize_row<MODE>(A, r, *reinterpret_cast<FinSmem*>(dyn_smem));
     } else if (tid == 0) {  // a wait of this call ran out: the row has no id
       A.out_ids[r] = -1;
       if (A.d_row_flags) A.d_row_flags[r] = MS_ROW_TIMEOUT;
@@ -1391,9 +1394,9 @@ constexpr size_t kResSmem = sizeof(ResSmem) > sizeof(FullSmem) ? sizeof(ResSmem)
 template <int MODE>
 constexpr size_t chunk_smem() { return MODE == kFull ? kSmemFull : kSmem; }
 
-template <int MODE, bool PEN>
+template <int MODE, bool PEN, bool FIN = false>
 cudaError_t set_attrs() {
-  return cudaFuncSetAttribute((const void*)sample_kernel<MODE, PEN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  return cudaFuncSetAttribute((const void*)sample_kernel<MODE, PEN, FIN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                               (int)chunk_smem<MODE>());
 }
 
@@ -1435,6 +1438,14 @@ cudaError_t set_fin_attrs() {
 
 template <int MODE, bool PEN>
 cudaError_t launch_mode(const Args& S, dim3 grid, cudaStream_t stream, cudaEvent_t mid) {
+  if constexpr (MODE == kTopK) {
+    if (S.fuse_fin) {  // one launch: the last chunk CTA of each row finalizes it
+      sample_kernel<MODE, PEN, true><<<grid, dim3(chunk_threads<MODE>()), chunk_smem<MODE>(), stream>>>(S);
+      cudaError_t e = cudaGetLastError();
+      if (mid) cudaEventRecord(mid, stream);
+      return e;
+    }
+  }
   sample_kernel<MODE, PEN><<<grid, dim3(chunk_threads<MODE>()), chunk_smem<MODE>(), stream>>>(S);
   cudaError_t e = cudaGetLastError();
   if (mid) cudaEventRecord(mid, stream);
@@ -1570,6 +1581,8 @@ cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev, i
     if (e == cudaSuccess) e = set_attrs<kGreedy, true>();
     if (e == cudaSuccess) e = set_attrs<kTopK, false>();
     if (e == cudaSuccess) e = set_attrs<kTopK, true>();
+    if (e == cudaSuccess) e = set_attrs<kTopK, false, true>();
+    if (e == cudaSuccess) e = set_attrs<kTopK, true, true>();
     if (e == cudaSuccess) e = set_attrs<kFull, false>();
     if (e == cudaSuccess) e = set_attrs<kFull, true>();
     if (e == cudaSuccess) e = set_fin_attrs<kTopK, 256>();
@@ -1608,6 +1621,9 @@ cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev, i
     if (A.d_row_flags) S.d_row_flags = A.d_row_flags + r0;
     const dim3 grid(rows, A.n_chunks);
     const bool pen = A.use_pen != 0;
+    // small top-k batches: the finalize in the chunk kernel saves the second
+    // launch; larger ones keep it as its own one-wave grid
+    S.fuse_fin = (A.mode == kTopK && rows <= kFuseRows) ? 1 : 0;
     const bool prof = ev != nullptr && r0 == 0;
     if (prof) cudaEventRecord(ev[0], stream);
     cudaEvent_t mid = prof ? ev[1] : nullptr;
@@ -1628,7 +1644,7 @@ cudaError_t launch_sample(const Args& A, cudaStream_t stream, cudaEvent_t* ev, i
     }
     if (prof) cudaEventRecord(ev[2], stream);
     if (e != cudaSuccess) return e;
-    if (launched) *launched += (A.mode == kGreedy) ? 1 : (A.mode == kFull ? 4 : 2);
+    if (launched) *launched += (A.mode == kGreedy || S.fuse_fin) ? 1 : (A.mode == kFull ? 4 : 2);
   }
   return cudaSuccess;
 }

@@ -37,13 +37,19 @@ def test_wait_timeout_fails_the_call_and_the_next_call_is_clean(oracle):
             s.sample(X, sp, u=u)
         assert e.value.code == N.MS_ERR_TIMEOUT
         np.testing.assert_array_equal(s.sample(X, sp, u=u), ref)
-        # asynchronous device call: the rows come back -1 (MS_ROW_TIMEOUT)
+        # asynchronous device call: the rows come back -1 (MS_ROW_TIMEOUT); in
+        # this small top-k call, which finalizes each row as its chunks finish,
+        # always row 0 (whose wait ran out), and any row finalized after it;
+        # the others keep their correct ids
         xd, ud = torch.from_numpy(X).cuda(), torch.from_numpy(u).cuda()
         s.inject(N.MS_INJECT_WAIT, 4000)
         ids, d = s.sample(xd, sp, u=ud, sync=False, diag=True)
         torch.cuda.synchronize()
-        assert ids.cpu().numpy().tolist() == [-1] * X.shape[0]
-        assert np.all(d["row_flags"].cpu().numpy() & N.MS_ROW_TIMEOUT)
+        ids = ids.cpu().numpy()
+        timed = (d["row_flags"].cpu().numpy() & N.MS_ROW_TIMEOUT) != 0
+        assert timed[0]
+        assert np.all(ids[timed] == -1)
+        np.testing.assert_array_equal(ids[~timed], ref[~timed])
         # the next asynchronous call is unaffected, and so is a synchronous one
         ids = s.sample(xd, sp, u=ud, sync=False)
         torch.cuda.synchronize()
@@ -54,6 +60,26 @@ def test_wait_timeout_fails_the_call_and_the_next_call_is_clean(oracle):
         with pytest.raises(N.MiniSampleError) as e:
             s.sample(xd, sp, u=ud, sync=True)
         assert e.value.code == N.MS_ERR_TIMEOUT
+        np.testing.assert_array_equal(s.sample(X, sp, u=u), ref)
+
+
+def test_wait_timeout_with_a_finalize_grid(oracle):
+    """Top-k calls of more than 16 rows finalize in a second grid, after every
+    chunk: a wait that ran out leaves every row of the call at -1."""
+    import torch
+
+    from minisample import Sampler
+    from minisample import _native as N
+
+    X, sp, u = _small(6, B=24)
+    ref, _ = oracle.sample_batch(X, None, None, params(oracle, sp), u)
+    with Sampler() as s:
+        xd, ud = torch.from_numpy(X).cuda(), torch.from_numpy(u).cuda()
+        s.inject(N.MS_INJECT_WAIT, 4000)
+        ids, d = s.sample(xd, sp, u=ud, sync=False, diag=True)
+        torch.cuda.synchronize()
+        assert ids.cpu().numpy().tolist() == [-1] * X.shape[0]
+        assert np.all(d["row_flags"].cpu().numpy() & N.MS_ROW_TIMEOUT)
         np.testing.assert_array_equal(s.sample(X, sp, u=u), ref)
 
 
